@@ -1,0 +1,48 @@
+// Python bindings of the runtime and kernel launchers (module deepep_trn_b200._C).
+#include <torch/extension.h>
+
+#include "ops.h"
+
+namespace py = pybind11;
+using namespace b200ep;
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels and NVLink symmetric-heap runtime of deepep_trn_b200";
+  py::class_<SymmHeap>(m, "SymmHeap")
+      .def(py::init<int, int, int, int, int, int, int, int, double>(), py::arg("rank"), py::arg("world"),
+           py::arg("max_tokens"), py::arg("max_ll_tokens"), py::arg("hidden"), py::arg("topk"),
+           py::arg("num_experts"), py::arg("device"), py::arg("timeout_s"))
+      .def("ipc_handle", [](const SymmHeap& h) { return py::bytes(h.ipc_handle()); })
+      .def("open", [](SymmHeap& h, const std::vector<py::bytes>& hs) {
+        std::vector<std::string> v;
+        for (auto& b : hs) v.emplace_back(std::string(b));
+        h.open(v);
+      })
+      .def("close", &SymmHeap::close)
+      .def("status", &SymmHeap::status)
+      .def("clear_status", &SymmHeap::clear_status)
+      .def("wait_notify", &SymmHeap::wait_notify, py::call_guard<py::gil_scoped_release>())
+      .def_property_readonly("rank", &SymmHeap::rank)
+      .def_property_readonly("world", &SymmHeap::world)
+      .def_property_readonly("num_sms", &SymmHeap::num_sms)
+      .def_property_readonly("total_bytes", &SymmHeap::total_bytes)
+      .def_property_readonly("is_open", &SymmHeap::is_open)
+      .def_property_readonly("config", [](const SymmHeap& h) {
+        const auto& c = h.config();
+        return py::make_tuple(c.R, c.M, c.Mll, c.H, c.K, c.E);
+      });
+  m.def("heap_bytes", [](int R, int M, int Mll, int H, int K, int E) {
+    return make_layout(HeapConfig{R, M, Mll, H, K, E}).total;
+  });
+  m.def("layout", &layout);
+  m.def("nd_prepare", &nd_prepare);
+  m.def("nd_pull", &nd_pull);
+  m.def("nc_combine", &nc_combine);
+  m.def("ll_dispatch_send", &ll_dispatch_send);
+  m.def("ll_dispatch_recv", &ll_dispatch_recv);
+  m.def("ll_combine_send", &ll_combine_send);
+  m.def("ll_combine_recv", &ll_combine_recv);
+  m.def("quant_fp8", &quant_fp8);
+  m.def("device_barrier", &device_barrier);
+  m.def("wait_probe", &wait_probe);
+}

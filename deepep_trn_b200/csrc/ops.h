@@ -1,0 +1,87 @@
+// Host-side declarations of the runtime and every kernel launcher exported to Python.
+#pragma once
+
+#include <atomic>
+#include <chrono>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include <ATen/ATen.h>
+#include <c10/util/Optional.h>
+
+#include "heap.cuh"
+
+namespace b200ep {
+
+class SymmHeap {
+ public:
+  SymmHeap(int rank, int world, int M, int Mll, int H, int K, int E, int device, double timeout_s);
+  ~SymmHeap();
+  SymmHeap(const SymmHeap&) = delete;
+  SymmHeap& operator=(const SymmHeap&) = delete;
+
+  std::string ipc_handle() const;
+  void open(const std::vector<std::string>& handles);
+  void close();
+  HeapView view() const;
+  std::vector<int64_t> status() const;
+  void clear_status();
+  std::vector<int64_t> wait_notify(uint64_t ticket, int num_local_experts, double timeout_s) const;
+
+  int rank() const { return rank_; }
+  int world() const { return world_; }
+  int device() const { return device_; }
+  int num_sms() const { return num_sms_; }
+  int64_t total_bytes() const { return layout_.total; }
+  const HeapConfig& config() const { return cfg_; }
+  bool is_open() const { return local_ != nullptr; }
+
+ private:
+  int rank_, world_, device_, num_sms_ = 0;
+  HeapConfig cfg_{};
+  HeapLayout layout_{};
+  uint64_t timeout_ns_ = 0;
+  void* local_ = nullptr;
+  std::vector<void*> peers_;
+  HostPage* host_ = nullptr;
+  HostPage* host_dev_ = nullptr;
+  bool opened_ = false;
+};
+
+using OptTensor = c10::optional<at::Tensor>;
+
+// layout.cu
+void layout(const at::Tensor& topk_idx, int64_t num_experts, int64_t num_ranks, at::Tensor ntr, at::Tensor nte,
+            at::Tensor itr, at::Tensor scratch);
+
+// normal.cu
+void nd_prepare(SymmHeap& heap, const at::Tensor& x, const OptTensor& x_scales, int64_t mode, bool round_scale,
+                const OptTensor& topk_idx, const OptTensor& topk_w, const at::Tensor& in_rank, at::Tensor token_pos,
+                at::Tensor recv_off, int64_t num_experts, int64_t ticket, int64_t num_sms);
+void nd_pull(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_scales, const OptTensor& recv_topk,
+             const OptTensor& recv_w, at::Tensor recv_src, int64_t mode, int64_t num_experts, int64_t num_sms,
+             bool use_tma);
+void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const at::Tensor& recv_off,
+                const at::Tensor& token_pos, at::Tensor out, const OptTensor& out_w, const OptTensor& bias0,
+                const OptTensor& bias1, int64_t num_sms);
+
+// ll.cu
+void ll_dispatch_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& topk_idx, int64_t num_experts,
+                      bool use_fp8, bool round_scale, int64_t num_sms);
+void ll_dispatch_recv(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_scales, at::Tensor recv_count,
+                      at::Tensor src_info, at::Tensor layout_range, at::Tensor pair_meta, int64_t num_experts,
+                      bool use_fp8, bool ue8m0, const OptTensor& cum_stats, const OptTensor& wait_stats);
+void ll_combine_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& recv_count, const at::Tensor& src_info,
+                     const at::Tensor& pair_meta, int64_t num_experts, int64_t num_sms);
+void ll_combine_recv(SymmHeap& heap, const at::Tensor& topk_idx, const at::Tensor& topk_w, at::Tensor out,
+                     int64_t num_sms);
+
+// diag.cu
+void device_barrier(SymmHeap& heap);
+void wait_probe(SymmHeap& heap, int64_t budget_ns);
+
+// quant.cu
+void quant_fp8(const at::Tensor& x, at::Tensor q, at::Tensor scales, bool round_scale);
+
+}  // namespace b200ep

@@ -1,0 +1,326 @@
+"""NVLink engine: drives the sm_100a kernels over the IPC-mapped symmetric heap.
+
+One op = one or two kernel launches on the caller's stream:
+
+  get_dispatch_layout  -> layout kernel (N1), no host round trip
+  dispatch             -> nd_prepare (stage / quantise / scan / count exchange),
+                          host waits on a host-mapped ticket for the receive size
+                          (skipped for a cached dispatch or with num_worst_tokens),
+                          nd_pull (receivers pull their rows with TMA bulk copies)
+  combine              -> nc_combine (push home + fp32 reduce, one cooperative kernel)
+  low_latency_dispatch -> ll_dispatch_send [+ ll_dispatch_recv, or via the hook]
+  low_latency_combine  -> ll_combine_send  [+ ll_combine_recv, or via the hook]
+
+Low-latency ops never touch the host and are CUDA-graph capturable once the
+heap exists (call them once before capture).
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+import torch.distributed as dist
+
+from ..handles import DispatchHandle, EventOverlap, LowLatencyHandle
+from ..ops._ext import load
+from ..utils.layout import experts_per_rank
+from ..utils.profiling import timer
+from .symm import HeapSpec, create_heap
+
+ERRORS = {1: 'timeout waiting for a peer to stage dispatch data', 2: 'timeout waiting for combine rows',
+          3: 'low-latency: timeout waiting for a source header', 4: 'low-latency: timeout waiting for a row',
+          5: 'low-latency combine: timeout waiting for a (token, k) row', 6: 'capacity exceeded',
+          7: 'timeout in device barrier', 8: 'bad input'}
+
+
+class DeviceError(RuntimeError):
+    pass
+
+
+class NvlinkEngine:
+    def __init__(self, group, num_max_tokens_per_rank: int, timeout_s: float, spec_hint: HeapSpec | None = None):
+        self.C = load()
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.R = dist.get_world_size(group)
+        self.M = num_max_tokens_per_rank
+        self.timeout_s = timeout_s
+        self.host_timeout_s = max(4 * timeout_s, 60.0)
+        self.heap = None
+        self.spec: HeapSpec | None = None
+        self.ticket = 0
+        self._scratch = None
+        self._ll_pending = False
+        self._lc_pending = False
+        self.last_exchange = None
+        if spec_hint is not None:
+            self._ensure(spec_hint)
+
+    # ------------------------------------------------------------------ heap
+    def _ensure(self, spec: HeapSpec) -> None:
+        if self.heap is not None and self.spec.covers(spec):
+            return
+        new = spec if self.spec is None else self.spec.merge(spec)
+        if self.heap is not None:
+            torch.cuda.synchronize()
+            if self.R > 1:
+                dist.barrier(group=self.group)
+            self.heap.close()
+        self.heap = create_heap(self.group, new, self.timeout_s)
+        self.spec = new
+
+    def check(self) -> None:
+        """Raise if any kernel of this buffer reported a device-side error."""
+        if self.heap is None:
+            return
+        code, op, rank, peer, expected, seen, aux = self.heap.status()
+        if code:
+            self.heap.clear_status()
+            raise DeviceError(f'{ERRORS.get(code, "device error")} (code={code} op={op} rank={rank} '
+                              f'peer={peer} expected={expected} seen={seen} aux={aux})')
+
+    def barrier(self) -> None:
+        """Device-side barrier over the EP group (epoch flags in peer memory, bounded wait)."""
+        if self.heap is not None:
+            self.C.device_barrier(self.heap)
+
+    def probe_timeout(self, timeout_ns: int) -> list:
+        """Run one bounded wait on a flag that nothing sets; returns the status it left."""
+        self.C.wait_probe(self.heap, int(timeout_ns))
+        torch.cuda.synchronize()
+        st = self.heap.status()
+        self.heap.clear_status()
+        return st
+
+    def destroy(self) -> None:
+        if self.heap is not None:
+            torch.cuda.synchronize()
+            if self.R > 1:
+                dist.barrier(group=self.group)
+            self.heap.close()
+            self.heap = None
+
+    def _sms(self, config) -> int:
+        from ..buffer import Buffer
+        n = getattr(config, 'num_sms', 0) if config is not None else 0
+        return int(n or Buffer.num_sms or 0)
+
+    def _spec(self, H, K, E, Mll=None) -> HeapSpec:
+        cur = self.spec
+        return HeapSpec(self.M, Mll if Mll is not None else (cur.max_ll_tokens if cur else 1), H, K, E)
+
+    # ------------------------------------------------------------------ layout
+    def get_dispatch_layout(self, topk_idx, num_experts):
+        experts_per_rank(num_experts, self.R)
+        T = topk_idx.shape[0]
+        dev = topk_idx.device
+        need = self.R + num_experts + 1
+        if self._scratch is None or self._scratch.numel() < need or self._scratch.device != dev:
+            self._scratch = torch.zeros(need, dtype=torch.int32, device=dev)
+        ntr = torch.empty(self.R, dtype=torch.int32, device=dev)
+        nte = torch.empty(num_experts, dtype=torch.int32, device=dev)
+        itr = torch.empty(T, self.R, dtype=torch.bool, device=dev)
+        with timer.stage('layout'):
+            self.C.layout(topk_idx.contiguous(), num_experts, self.R, ntr, nte, itr, self._scratch)
+        return ntr, nte, itr
+
+    # ------------------------------------------------------------------ normal mode
+    def dispatch(self, x, handle, topk_idx, topk_weights, is_token_in_rank, num_experts, expert_alignment,
+                 num_worst_tokens, config, use_fp8=False, round_scale=False):
+        self.check()
+        fp8_in = isinstance(x, tuple)
+        xt = x[0] if fp8_in else x
+        T, H = xt.shape
+        dev = xt.device
+        cached = handle is not None
+        if cached:
+            K, E, itr = handle.topk, handle.num_experts, handle.is_token_in_rank
+        else:
+            K = topk_idx.shape[1]
+            E = num_experts
+            itr = is_token_in_rank if is_token_in_rank is not None else self.get_dispatch_layout(topk_idx, E)[2]
+        EL = experts_per_rank(E, self.R)
+        self._ensure(self._spec(H, K, E))
+        mode = 1 if fp8_in else (2 if use_fp8 else 0)
+        token_pos = torch.empty(T, self.R, dtype=torch.int32, device=dev)
+        recv_off = torch.empty(self.R + 1, dtype=torch.int64, device=dev)
+        self.ticket += 1
+        nsm = self._sms(config)
+        with timer.stage('prepare'):
+            self.C.nd_prepare(self.heap, xt if not fp8_in else xt.view(torch.uint8),
+                              x[1].float().contiguous() if fp8_in else None, mode, bool(round_scale),
+                              None if cached else topk_idx.contiguous(),
+                              None if (cached or topk_weights is None) else topk_weights.float().contiguous(),
+                              itr.contiguous(), token_pos, recv_off, E, self.ticket, nsm)
+        # Outputs are sized for the worst case (every peer sends its full capacity) so the pull
+        # kernel can be queued before the host learns the receive size; the host then waits
+        # on the notify ticket while the GPU is already pulling, and returns the first N rows.
+        if num_worst_tokens:
+            cap = int(num_worst_tokens)
+        elif cached:
+            cap = handle.num_recv if handle.num_recv is not None else handle.capacity
+        else:
+            cap = self.R * self.M
+        if mode == 0:
+            recv_x = torch.empty(cap, H, dtype=xt.dtype, device=dev)
+            recv_s = None
+        else:
+            recv_x = torch.empty(cap, H, dtype=torch.float8_e4m3fn, device=dev)
+            recv_s = torch.empty(cap, H // 128, dtype=torch.float32, device=dev)
+        recv_topk = recv_w = None
+        if not cached:
+            recv_topk = torch.empty(cap, K, dtype=topk_idx.dtype, device=dev)
+            if topk_weights is not None:
+                recv_w = torch.empty(cap, K, dtype=torch.float32, device=dev)
+        recv_src = torch.empty(cap, dtype=torch.int64, device=dev)
+        use_tma = True if config is None else bool(getattr(config, 'use_tma', True))
+        if os.environ.get('B200EP_NO_TMA'):
+            use_tma = False
+        with timer.stage('pull'):
+            self.C.nd_pull(self.heap, recv_x, recv_s, recv_topk, recv_w, recv_src, mode, E, nsm, use_tma)
+        per_expert = recv_counts = None
+        if num_worst_tokens or cached:
+            N = cap
+            recv_counts = handle.recv_counts if cached else None
+        else:
+            with timer.stage('notify_wait'):
+                info = self.heap.wait_notify(self.ticket, EL, self.host_timeout_s)
+            N = int(info[0])
+            recv_counts = torch.tensor(info[1:1 + self.R], dtype=torch.int64)
+            per_expert = info[1 + self.R:1 + self.R + EL]
+            if expert_alignment > 1:
+                per_expert = [(c + expert_alignment - 1) // expert_alignment * expert_alignment for c in per_expert]
+            recv_x, recv_src = recv_x[:N], recv_src[:N]
+            recv_s = recv_s[:N] if recv_s is not None else None
+            recv_topk = recv_topk[:N]
+            recv_w = recv_w[:N] if recv_w is not None else None
+        new = DispatchHandle(T, K, None, recv_counts, recv_src, itr, num_recv=None if num_worst_tokens else N,
+                             token_pos=token_pos, recv_off=recv_off, hidden=H, num_experts=E)
+        new.capacity = cap
+        self.last_exchange = dict(mode='normal', rows=N, hidden=H, payload_bytes=(2 * H if mode == 0 else H + H // 32))
+        out_x = recv_x if mode == 0 else (recv_x, recv_s)
+        if cached:
+            return out_x, None, None, None, new, EventOverlap()
+        if recv_w is not None and topk_weights.dtype != torch.float32:
+            recv_w = recv_w.to(topk_weights.dtype)
+        return out_x, recv_topk, recv_w, per_expert, new, EventOverlap()
+
+    def combine(self, x, handle, topk_weights, bias, config):
+        self.check()
+        N, H = x.shape
+        if handle.num_recv is not None and N != handle.num_recv:
+            raise ValueError(f'combine got {N} rows, dispatch delivered {handle.num_recv}')
+        if x.dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError(f'combine needs bf16/fp16 rows, got {x.dtype}')
+        K = topk_weights.shape[1] if topk_weights is not None else handle.topk
+        self._ensure(self._spec(H, K, handle.num_experts))
+        T = handle.num_tokens
+        out = torch.empty(T, H, dtype=x.dtype, device=x.device)
+        out_w = torch.empty(T, topk_weights.shape[1], dtype=torch.float32, device=x.device) \
+            if topk_weights is not None else None
+        b = [t.contiguous() for t in bias]
+        with timer.stage('combine'):
+            self.C.nc_combine(self.heap, x if x.stride(1) == 1 else x.contiguous(),
+                              topk_weights.float().contiguous() if topk_weights is not None else None,
+                              handle.recv_off, handle.token_pos, out, out_w,
+                              b[0] if len(b) > 0 else None, b[1] if len(b) > 1 else None, self._sms(config))
+        if out_w is not None and topk_weights.dtype != torch.float32:
+            out_w = out_w.to(topk_weights.dtype)
+        return out, out_w, EventOverlap()
+
+    # ------------------------------------------------------------------ low latency
+    def low_latency_dispatch(self, x, topk_idx, M, num_experts, use_fp8, round_scale, use_ue8m0,
+                             cumulative_stats, wait_stats, return_recv_hook):
+        self.check()
+        if self._ll_pending:
+            raise RuntimeError('call the previous low_latency_dispatch recv hook before dispatching again')
+        T, H = x.shape
+        K = topk_idx.shape[1]
+        R = self.R
+        EL = experts_per_rank(num_experts, R)
+        self._ensure(self._spec(H, K, num_experts, Mll=M))
+        Mll = self.spec.max_ll_tokens
+        dev = x.device
+        with timer.stage('ll_send'):
+            self.C.ll_dispatch_send(self.heap, x, topk_idx.contiguous(), num_experts, bool(use_fp8),
+                                    bool(round_scale or use_ue8m0), self._sms(None))
+        if use_fp8:
+            recv_x = torch.empty(EL, R * Mll, H, dtype=torch.float8_e4m3fn, device=dev)
+            recv_s = torch.empty(EL, R * Mll, H // 128, dtype=torch.uint8 if use_ue8m0 else torch.float32, device=dev)
+        else:
+            recv_x = torch.empty(EL, R * Mll, H, dtype=x.dtype, device=dev)
+            recv_s = None
+        recv_count = torch.empty(EL, dtype=torch.int32, device=dev)
+        src_info = torch.empty(EL, R * Mll, dtype=torch.int32, device=dev)
+        layout_range = torch.empty(EL, R, dtype=torch.int64, device=dev)
+        pair_meta = torch.empty(EL, R * Mll, dtype=torch.int32, device=dev)
+        cum = cumulative_stats if (cumulative_stats is not None and cumulative_stats.dtype == torch.int32) else None
+
+        def recv():
+            with timer.stage('ll_recv'):
+                self.C.ll_dispatch_recv(self.heap, recv_x, recv_s, recv_count, src_info, layout_range, pair_meta,
+                                        num_experts, bool(use_fp8), bool(use_ue8m0), cum, wait_stats)
+            if cumulative_stats is not None and cum is None:
+                cumulative_stats.add_(recv_count.to(cumulative_stats.dtype))
+            self._ll_pending = False
+
+        n = R * M
+        if use_fp8:
+            s = recv_s[:, :n]
+            if use_ue8m0 and (H // 128) % 4 == 0:
+                s = recv_s.view(torch.int32)[:, :n]
+            packed = (recv_x[:, :n], s)
+        else:
+            packed = recv_x[:, :n]
+        handle = LowLatencyHandle(T, M, H, num_experts, K, src_info[:, :n], layout_range, recv_count,
+                                  pair_meta=pair_meta, use_fp8=bool(use_fp8),
+                                  extra=dict(src_info_full=src_info, pair_meta_full=pair_meta))
+        self.last_exchange = dict(mode='ll', tokens=T, hidden=H)
+        self._ll_pending = True
+        hook = None
+        if return_recv_hook:
+            hook = _OneShot(recv)
+        else:
+            recv()
+        return packed, recv_count, handle, EventOverlap(), hook
+
+    def low_latency_combine(self, x, topk_idx, topk_weights, handle, zero_copy, return_recv_hook, out):
+        self.check()
+        if self._lc_pending:
+            raise RuntimeError('call the previous low_latency_combine recv hook before combining again')
+        if self._ll_pending:
+            raise RuntimeError('call the low_latency_dispatch recv hook before combining')
+        T, H = handle.num_tokens, handle.hidden
+        if x.dim() != 3 or x.shape[-1] != H:
+            raise ValueError(f'combine x must be [EL, R*M, {H}], got {tuple(x.shape)}')
+        with timer.stage('ll_send'):
+            self.C.ll_combine_send(self.heap, x, handle.recv_count, handle.extra['src_info_full'],
+                                   handle.extra['pair_meta_full'], handle.num_experts, self._sms(None))
+        result = out if out is not None else torch.empty(T, H, dtype=x.dtype, device=x.device)
+        idx = topk_idx.contiguous()
+        w = topk_weights.float().contiguous()
+
+        def recv():
+            with timer.stage('ll_recv'):
+                self.C.ll_combine_recv(self.heap, idx, w, result, self._sms(None))
+            self._lc_pending = False
+
+        self._lc_pending = True
+        hook = None
+        if return_recv_hook:
+            hook = _OneShot(recv)
+        else:
+            recv()
+        return result, EventOverlap(), hook
+
+
+class _OneShot:
+    """A receive hook: launches the receive kernel once (later calls are no-ops)."""
+
+    def __init__(self, fn):
+        self._fn = fn
+
+    def __call__(self) -> None:
+        if self._fn is not None:
+            fn, self._fn = self._fn, None
+            fn()

@@ -1,0 +1,65 @@
+"""Multi-process CPU tests over gloo: the full Buffer semantics without a GPU."""
+import pytest
+import torch
+import torch.distributed as dist
+
+
+@pytest.fixture(scope='module')
+def single_rank_group(tmp_path_factory):
+    path = tmp_path_factory.mktemp('pg') / 'store'
+    dist.init_process_group('gloo', init_method=f'file://{path}', rank=0, world_size=1)
+    yield dist.group.WORLD
+    dist.destroy_process_group()
+
+
+def test_single_rank_roundtrip(single_rank_group):
+    from deepep_trn_b200 import Buffer
+    g = torch.Generator().manual_seed(2)
+    T, H, E, K, M = 20, 128, 16, 4, 32
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    idx = torch.rand(T, E, generator=g).topk(K, dim=-1).indices
+    w = torch.rand(T, K, generator=g)
+    buf = Buffer(single_rank_group, backend='gloo', num_max_tokens_per_rank=M)
+    ntr, _, nte, itr, _ = buf.get_dispatch_layout(idx, E)
+    rx, ridx, rw, per_expert, handle, _ = buf.dispatch(
+        x, topk_idx=idx, topk_weights=w, num_tokens_per_rank=ntr, is_token_in_rank=itr, num_tokens_per_expert=nte)
+    assert torch.equal(rx, x) and torch.equal(ridx, idx) and torch.equal(rw, w)
+    assert per_expert == nte.tolist()
+    combined, cw, _ = buf.combine(rx, handle, topk_weights=rw)
+    assert torch.equal(combined, x) and torch.equal(cw, w)
+
+    recv_x, count, ll_handle, _, hook = buf.low_latency_dispatch(x, idx, M, E, use_fp8=False, return_recv_hook=True)
+    hook()
+    assert recv_x.shape == (E, M, H) and int(count.sum()) == T * K
+    out, _, _ = buf.low_latency_combine(recv_x, idx, w, ll_handle)
+    ref = (x.float() * w.sum(-1, keepdim=True)).to(torch.bfloat16)
+    assert torch.allclose(out.float(), ref.float(), rtol=1e-2, atol=1e-3)
+
+    (q, s), count, ll_handle, _, _ = buf.low_latency_dispatch(x, idx, M, E)  # fp8 by default
+    assert q.dtype == torch.float8_e4m3fn and s.shape == (E, M, H // 128)
+
+    with pytest.raises(ValueError):
+        buf.dispatch(torch.zeros(M + 1, H, dtype=torch.bfloat16), topk_idx=idx.repeat(2, 1)[:M + 1],
+                     num_tokens_per_expert=nte)
+    with pytest.raises(ValueError):
+        buf.dispatch(x, topk_idx=idx)  # missing num_tokens_per_expert
+    with pytest.raises(ValueError):
+        buf.combine(rx[:-1], handle)
+    with pytest.raises(NotImplementedError):
+        buf.low_latency_combine(recv_x, idx, w, ll_handle, use_logfmt=True)
+    with pytest.raises(ValueError):
+        Buffer(single_rank_group, backend='bogus')
+
+
+@pytest.mark.parametrize('ep', [4, 2])
+def test_intranode_gloo(run_dist, ep):
+    rc, out = run_dist('intranode.py', 4, '--backend', 'gloo', '--ep', ep, '--hidden', 256, '--experts', 32,
+                       '--topk', 4, timeout=600)
+    assert rc == 0 and 'INTRANODE_PASS' in out, out[-4000:]
+
+
+@pytest.mark.parametrize('ep', [4, 2])
+def test_low_latency_gloo(run_dist, ep):
+    rc, out = run_dist('low_latency.py', 4, '--backend', 'gloo', '--ep', ep, '--hidden', 256, '--experts', 32,
+                       '--topk', 4, timeout=600)
+    assert rc == 0 and 'LOW_LATENCY_PASS' in out, out[-4000:]

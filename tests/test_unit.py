@@ -1,0 +1,122 @@
+"""CPU unit tests: codec, layout math, fp8 codec, routing helpers, transports contract.
+
+Scenarios follow deep_ep_trn tests/unit/test_codec_layout.py.
+"""
+import pytest
+import torch
+
+from deepep_trn_b200 import RowCodec, get_dispatch_layout
+from deepep_trn_b200.utils.codec import (dequantize_fp8_1x128, float_to_ue8m0, fp8_error_bound, quantize_fp8_1x128,
+                                         ue8m0_to_float)
+from deepep_trn_b200.utils.layout import pair_plan, rank_of_expert, send_plan, slot_index, token_positions
+from deepep_trn_b200.utils.testing import (ROUTINGS, expected_distinct_ranks, make_routing, randn_router,
+                                           router_topk_reference, strided_ep_groups, zipf_router)
+
+
+def test_codec_roundtrip_is_bit_exact():
+    g = torch.Generator().manual_seed(0)
+    T, H, K = 37, 256, 8
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    idx = torch.randint(-1, 128, (T, K), generator=g)
+    w = torch.randn(T, K, generator=g)
+    w[0, 0], w[1, 1] = float('inf'), -0.0
+    token = torch.arange(T) * 1_000_003
+    codec = RowCodec(H, K)
+    assert codec.width % 32 == 0 and codec.width >= H + 4 * K + 2
+    rx, ridx, rw, rtok = codec.decode(codec.encode(x, idx, w, token))
+    assert torch.equal(rx.view(torch.int16), x.view(torch.int16))
+    assert torch.equal(ridx, idx) and torch.equal(rtok, token)
+    assert torch.equal(rw.view(torch.int32), w.view(torch.int32))
+    with pytest.raises(ValueError):
+        RowCodec(H, K, torch.float32)
+
+
+def test_layout_matches_naive():
+    g = torch.Generator().manual_seed(1)
+    T, E, K, R = 50, 64, 6, 4
+    idx = torch.rand(T, E, generator=g).topk(K, dim=-1).indices
+    idx[::7, 2] = -1
+    per_rank, per_expert, in_rank = get_dispatch_layout(idx, E, R)
+    naive = torch.zeros(T, R, dtype=torch.bool)
+    for t in range(T):
+        for e in idx[t].tolist():
+            if e >= 0:
+                naive[t, e // (E // R)] = True
+    assert torch.equal(in_rank, naive)
+    assert per_rank.dtype == torch.int32 and per_expert.dtype == torch.int32
+    assert torch.equal(per_rank.long(), naive.sum(0))
+    assert torch.equal(per_expert.long(), torch.bincount(idx[idx >= 0], minlength=E))
+    token, counts = send_plan(in_rank)
+    expected = torch.cat([naive[:, r].nonzero().flatten() for r in range(R)])
+    assert torch.equal(token, expected) and torch.equal(counts, naive.sum(0))
+    pos = token_positions(in_rank)
+    for r in range(R):
+        rows = naive[:, r].nonzero().flatten()
+        assert torch.equal(pos[rows, r].long(), torch.arange(rows.numel()))
+        assert (pos[~naive[:, r], r] == -1).all()
+    tok, kk, pcounts = pair_plan(rank_of_expert(idx, E, R), R)
+    assert int(pcounts.sum()) == int((idx >= 0).sum())
+    assert torch.equal(rank_of_expert(idx[tok, kk], E, R), torch.repeat_interleave(torch.arange(R), pcounts))
+    # (dst, token, k) order
+    keys = rank_of_expert(idx[tok, kk], E, R) * (T * K) + tok * K + kk
+    assert torch.equal(keys, keys.sort().values)
+    with pytest.raises(ValueError):
+        rank_of_expert(idx, 63, 4)
+
+
+def test_slot_index():
+    assert slot_index(torch.tensor([2, 0, 3]), 4).tolist() == [0, 1, 8, 9, 10]
+    assert slot_index(torch.tensor([0, 0]), 4).tolist() == []
+
+
+def test_fp8_codec_bounds_and_ue8m0():
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn(33, 512, generator=g) * torch.logspace(-3, 2, 512)).to(torch.bfloat16)
+    x[0] = 0
+    for rs in (False, True):
+        q, s = quantize_fp8_1x128(x, round_scale=rs)
+        assert q.dtype == torch.float8_e4m3fn and s.shape == (33, 4)
+        err = (dequantize_fp8_1x128(q, s) - x.float()).abs()
+        assert (err <= fp8_error_bound(x, s)).all()
+        if rs:
+            packed = float_to_ue8m0(s)
+            assert packed.dtype == torch.int32 and packed.shape == (33, 1)
+            assert torch.equal(ue8m0_to_float(packed, 512), s)
+            m = s.view(torch.int32) & 0x7FFFFF
+            assert (m == 0).all()
+    # amax floor keeps all-zero blocks finite
+    assert torch.isfinite(quantize_fp8_1x128(torch.zeros(2, 128))[1]).all()
+
+
+def test_testing_helpers():
+    assert strided_ep_groups(4, 2) == [[0, 2], [1, 3]] and strided_ep_groups(4, 4) == [[0, 1, 2, 3]]
+    assert strided_ep_groups(8, 2) == [[0, 4], [1, 5], [2, 6], [3, 7]]
+    with pytest.raises(ValueError):
+        strided_ep_groups(6, 4)
+    T, E, K, R = 24, 128, 8, 4
+    for kind in ROUTINGS:
+        for ep_rank in range(R):
+            idx, w = make_routing(kind, T, E, K, R, ep_rank, seed=ep_rank)
+            n = idx.shape[0]
+            assert idx.shape == (n, K) and w.shape == (n, K) and n <= T
+            assert not n or (int(idx.max()) < E and int(idx.min()) >= -1)
+            if kind not in ('masked', 'ragged'):
+                assert n == T and (idx >= 0).all()
+            if kind == 'hot_rank0':
+                assert (idx < E // R).all()
+            if n:
+                assert torch.allclose(w.sum(-1), torch.ones(n), atol=1e-5)
+    assert make_routing('ragged', T, E, K, R, R - 1, 0)[0].shape[0] == 0
+    assert abs(expected_distinct_ranks(256, 8, 8) - 5.295) < 1e-3
+
+
+def test_routers():
+    idx, w = randn_router(64, 256, 8, seed=0)
+    assert idx.shape == (64, 8) and torch.allclose(w.sum(-1), torch.ones(64))
+    assert all(len(set(r)) == 8 for r in idx.tolist())
+    zi, _ = zipf_router(4096, 256, 8, seed=1)
+    counts = torch.bincount(zi.flatten(), minlength=256)
+    assert counts.max() > 4 * counts.float().mean()  # skewed
+    logits = torch.tensor([[1.0, 3.0, 2.0, 3.0]])
+    i, ww = router_topk_reference(logits, 2)
+    assert sorted(i[0].tolist()) == [1, 3]
