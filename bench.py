@@ -55,6 +55,7 @@ def parse():
     p.add_argument('--no-ll', action='store_true')
     p.add_argument('--no-e2e', action='store_true')
     p.add_argument('--fp8', action='store_true', help='quantise to fp8 1x128 inside dispatch (config 3)')
+    p.add_argument('--profile', action='store_true', help='print a per-kernel breakdown (torch.profiler) to stderr')
     return p.parse_args()
 
 
@@ -156,6 +157,9 @@ def main():
     value = agg_bytes / (ms_step * 1e-3) / 1e9
     offrank = sum_over_ranks(offrank_bytes_rank) / (ms_step * 1e-3) / 1e9
 
+    if args.profile:
+        profile_steps(lambda: step(x, idx, w), 'normal d+c', rank)
+
     # ---- end to end through the public API: pinned H2D of inputs, D2H of the combined result
     e2e = None
     if not args.no_e2e:
@@ -215,6 +219,19 @@ def main():
     dist.destroy_process_group()
 
 
+def profile_steps(fn, label, rank, n=3):
+    from torch.profiler import ProfilerActivity, profile
+    from deepep_trn_b200.utils.benchutil import log
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(n):
+            fn()
+        torch.cuda.synchronize()
+    if rank == 0:
+        log(f'---- kernel breakdown: {label} ({n} steps, profiler timings, not bench numbers)')
+        log(prof.key_averages().table(sort_by='cuda_time_total', row_limit=15))
+
+
 def bench_ll(args, buf, rank, dev, control):
     from deepep_trn_b200.utils.benchutil import max_over_ranks
     from deepep_trn_b200.utils.testing import randn_router
@@ -233,6 +250,8 @@ def bench_ll(args, buf, rank, dev, control):
     for _ in range(3):
         ll_step()
     torch.cuda.synchronize()
+    if args.profile:
+        profile_steps(ll_step, 'low-latency fp8 d + bf16 c', rank)
     graph = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())

@@ -207,7 +207,8 @@ class Buffer:
         num_experts = handle.num_experts if cached else num_tokens_per_expert.numel()
         if self.backend == 'nvlink':
             fn = lambda: self._engine.dispatch(x, handle, topk_idx, topk_weights, is_token_in_rank, num_experts,
-                                               expert_alignment, num_worst_tokens, config, use_fp8, round_scale)
+                                               expert_alignment, num_worst_tokens, config, use_fp8, round_scale,
+                                               num_tokens_per_expert)
         else:
             if num_worst_tokens:
                 raise NotImplementedError('num_worst_tokens needs the nvlink backend')

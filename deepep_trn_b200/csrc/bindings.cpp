@@ -44,5 +44,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ll_combine_recv", &ll_combine_recv);
   m.def("quant_fp8", &quant_fp8);
   m.def("device_barrier", &device_barrier);
+  m.def("grouped_gemm_m", &grouped_gemm_m);
+  m.def("router_topk", &router_topk);
+  m.def("router_topk_bwd", &router_topk_bwd);
+  m.def("permute", &permute);
+  m.def("unpermute", &unpermute);
+  m.def("unpermute_bwd", &unpermute_bwd);
+  m.def("permute_bwd", &permute_bwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("transpose", &transpose);
+  m.def("grouped_gemm_k", &grouped_gemm_k);
   m.def("wait_probe", &wait_probe);
 }

@@ -161,6 +161,7 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
 }
 
 // Copy n bytes with one warp, using the widest access both pointers allow.
+// The 16-byte path keeps eight loads per lane in flight (4 KB per warp).
 __device__ __forceinline__ void warp_copy(void* __restrict__ dst, const void* __restrict__ src, int64_t n) {
   const int lane = lane_id();
   const uintptr_t a = reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src);
@@ -169,9 +170,12 @@ __device__ __forceinline__ void warp_copy(void* __restrict__ dst, const void* __
     int4* d = reinterpret_cast<int4*>(dst);
     const int4* s = reinterpret_cast<const int4*>(src);
     int64_t i = lane;
-    for (; i + 96 < m; i += 128) {  // four 16-byte loads in flight per lane
-      int4 v0 = s[i], v1 = s[i + 32], v2 = s[i + 64], v3 = s[i + 96];
-      d[i] = v0; d[i + 32] = v1; d[i + 64] = v2; d[i + 96] = v3;
+    for (; i + 224 < m; i += 256) {
+      int4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = s[i + 32 * u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) d[i + 32 * u] = v[u];
     }
     for (; i < m; i += 32) d[i] = s[i];
   } else if ((a & 3) == 0 && (n & 3) == 0) {
@@ -182,6 +186,21 @@ __device__ __forceinline__ void warp_copy(void* __restrict__ dst, const void* __
     for (int64_t i = lane; i < n; i += 32)
       reinterpret_cast<uint8_t*>(dst)[i] = reinterpret_cast<const uint8_t*>(src)[i];
   }
+}
+
+// Copy n bytes (multiple of 16, both ends 16-byte aligned) with a whole CTA,
+// four 16-byte loads per thread in flight.
+__device__ __forceinline__ void cta_copy16(void* __restrict__ dst, const void* __restrict__ src, int64_t n) {
+  const int64_t m = n >> 4;
+  int4* d = reinterpret_cast<int4*>(dst);
+  const int4* s = reinterpret_cast<const int4*>(src);
+  const int nt = blockDim.x;
+  int64_t i = threadIdx.x;
+  for (; i + 3 * nt < m; i += 4 * nt) {
+    int4 v0 = s[i], v1 = s[i + nt], v2 = s[i + 2 * nt], v3 = s[i + 3 * nt];
+    d[i] = v0; d[i + nt] = v1; d[i + 2 * nt] = v2; d[i + 3 * nt] = v3;
+  }
+  for (; i < m; i += nt) d[i] = s[i];
 }
 
 // ----------------------------------------------------------------------------- mbarrier + TMA bulk
@@ -301,19 +320,26 @@ __device__ __forceinline__ void load8(float (&v)[8], const T16* p, bool act) {
 }
 
 // Quantise one row of bf16/fp16 into [H fp8 | H/128 fp32 scales] with one warp (H % 128 == 0).
+// Four 256-element chunks are loaded before any is quantised (four loads in flight per lane).
 template <typename T16>
 __device__ __forceinline__ void warp_quant_row(uint8_t* __restrict__ dst, float* __restrict__ scales,
                                                const T16* __restrict__ src, int H, bool round_scale) {
   const int lane = lane_id();
-  for (int c = 0; c < H; c += 256) {
-    const int off = c + lane * 8;
-    const bool act = off < H;
-    float v[8];
-    load8(v, src + off, act);
-    const Quant8 r = quant8_e4m3(v, round_scale);
-    if (act) {
-      *reinterpret_cast<uint2*>(dst + off) = r.q;
-      if ((lane & 15) == 0) scales[off / 128] = r.scale;
+  for (int c0 = 0; c0 < H; c0 += 1024) {
+    float v[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int off = c0 + u * 256 + lane * 8;
+      load8(v[u], src + off, off < H);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int off = c0 + u * 256 + lane * 8;
+      const Quant8 r = quant8_e4m3(v[u], round_scale);
+      if (off < H) {
+        *reinterpret_cast<uint2*>(dst + off) = r.q;
+        if ((lane & 15) == 0) scales[off / 128] = r.scale;
+      }
     }
   }
 }

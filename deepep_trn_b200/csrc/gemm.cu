@@ -1,0 +1,483 @@
+// N7 / N8: grouped expert GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+//   GROUP_M:  C[off_e : off_e+m_e, :] = A[off_e : off_e+m_e, :] @ B[e]^T      (forward, dX)
+//   GROUP_K:  C[e] = A[:, off_e : off_e+m_e] @ B[:, off_e : off_e+m_e]^T          (dW)
+//
+// A, B are bf16 and K-major (the reduction dimension is contiguous). Expert
+// segments are padded to multiples of 128 rows (the permute kernel does this),
+// so every M tile (GROUP_M) or K block (GROUP_K) lies inside one expert.
+//
+// Per CTA (one per SM, persistent over tiles), 6 warps:
+//   warp 0      TMA producer: one elected thread streams A/B k-blocks (128B-swizzled
+//               boxes, no multicast) into a STAGES-deep shared-memory ring.
+//   warp 1      TMEM owner + MMA issuer: allocates 512 TMEM columns (two 128x256
+//               fp32 accumulators), one elected thread issues tcgen05.mma
+//               (M=128, N=BN, K=16) per 16-wide k slice and commits each stage
+//               back to the producer and each finished tile to the epilogue.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (thread = row), fused
+//               activation (SwiGLU on interleaved gate/up blocks) and the bf16/fp32
+//               cast, stores to global, then frees the accumulator.
+// Every mbarrier wait is bounded; on timeout the CTA records an error, stops
+// issuing, frees its TMEM and returns.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "ops.h"
+
+namespace b200ep {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;           // 64 bf16 = 128 bytes = one swizzle row
+constexpr int UMMA_K = 16;
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+
+enum Epilogue : int { kEpiBF16 = 0, kEpiF32 = 1, kEpiSwiGLU = 2 };
+
+struct Args {
+  const int64_t* offsets;   // [G + 1] row (GROUP_M) or token (GROUP_K) offsets, multiples of 128
+  int G;
+  int M, N, K;              // GROUP_M: N, K fixed, M = rows of A (bounds the offsets). GROUP_K: M, N fixed.
+  void* C;
+  int64_t ldc;              // elements
+  void* H;                  // SwiGLU output [rows, N/2] bf16
+  int64_t ldh;
+  int64_t c_group_stride;   // GROUP_K: elements between experts' outputs
+  uint32_t* error;          // device word, non-zero after a timeout
+  uint64_t timeout_ns;
+};
+
+// ----------------------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ void tma_load_2d(void* smem, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(smem)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// 32 lanes x 32 consecutive fp32 columns: thread i of the warp gets row (lane base + i).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128 bytes,
+// 8-row groups 1024 bytes apart (the layout a SWIZZLE_128B TMA box produces).
+__device__ __forceinline__ uint64_t smem_desc_k128(const void* p) {
+  const uint64_t addr = smem_u32(p);
+  uint64_t d = (addr >> 4) & 0x3FFFull;   // start address
+  d |= 1ull << 16;                         // leading byte offset (unused for swizzled K-major)
+  d |= (1024ull >> 4) << 32;               // stride byte offset: 8 rows x 128 B
+  d |= 1ull << 46;                         // descriptor version for sm_100
+  d |= 2ull << 61;                         // SWIZZLE_128B
+  return d;
+}
+// Instruction descriptor: D fp32, A/B bf16, both K-major, M=128, N=n.
+__host__ __device__ constexpr uint32_t idesc_bf16(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const Args& a) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_ns() - t0 > a.timeout_ns || *reinterpret_cast<volatile uint32_t*>(a.error) != 0u) {
+      atomicExch(a.error, 1u);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.f + __expf(-g)); }
+
+template <int BN>
+struct Smem {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+};
+
+// Tile t -> (group, m0 / k range, n0). Returns false past the end.
+struct Tile {
+  int g;
+  int m0, n0;
+  int kb0, nkb;  // k-block range
+};
+
+template <bool GROUP_K, int BN>
+__device__ __forceinline__ bool tile_of(int t, const Args& a, const int64_t* offs, Tile& tl) {
+  const int ntiles_n = (a.N + BN - 1) / BN;
+  if (!GROUP_K) {
+    const int total_m = static_cast<int>((offs[a.G] < a.M ? offs[a.G] : a.M) / BM);
+    if (t >= total_m * ntiles_n) return false;
+    const int mt = t / ntiles_n;
+    tl.n0 = (t % ntiles_n) * BN;
+    tl.m0 = mt * BM;
+    int lo = 0, hi = a.G - 1;  // last group with offs[g] <= m0
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (offs[mid] <= tl.m0) lo = mid; else hi = mid - 1;
+    }
+    tl.g = lo;
+    tl.kb0 = 0;
+    tl.nkb = (a.K + BK - 1) / BK;
+  } else {
+    const int ntiles_m = (a.M + BM - 1) / BM;
+    const int per = ntiles_m * ntiles_n;
+    if (t >= per * a.G) return false;
+    tl.g = t / per;
+    const int r = t % per;
+    tl.m0 = (r / ntiles_n) * BM;
+    tl.n0 = (r % ntiles_n) * BN;
+    tl.kb0 = static_cast<int>(offs[tl.g] / BK);
+    tl.nkb = static_cast<int>((offs[tl.g + 1] - offs[tl.g]) / BK);
+  }
+  return true;
+}
+
+template <bool GROUP_K, int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  using S = Smem<BN>;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * S::kBBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  __shared__ int64_t s_offs[1025];
+  __shared__ volatile int s_abort;
+
+  const int warp = warp_id(), lane = lane_id();
+  for (int i = threadIdx.x; i <= a.G && i <= 1024; i += kThreads) s_offs[i] = a.offsets[i];
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      Tile tl;
+      for (int t = blockIdx.x; tile_of<GROUP_K, BN>(t, a, s_offs, tl) && !s_abort; t += gridDim.x) {
+        for (int kb = 0; kb < tl.nkb; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!wait_bar(&empty[s], ((it / STAGES) & 1u) ^ 1u, a)) { s_abort = 1; break; }
+          mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+          const int kc = (tl.kb0 + kb) * BK;
+          if (!GROUP_K) {
+            tma_load_2d(sA + s * S::kABytes, &tmA, &full[s], kc, tl.m0);
+            tma_load_2d(sB + s * S::kBBytes, &tmB, &full[s], kc, tl.g * a.N + tl.n0);
+          } else {
+            tma_load_2d(sA + s * S::kABytes, &tmA, &full[s], kc, tl.m0);
+            tma_load_2d(sB + s * S::kBBytes, &tmB, &full[s], kc, tl.n0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(BN);
+      uint32_t it = 0, acc = 0;
+      Tile tl;
+      for (int t = blockIdx.x; tile_of<GROUP_K, BN>(t, a, s_offs, tl) && !s_abort; t += gridDim.x) {
+        if (tl.nkb == 0) continue;  // empty expert: the epilogue writes zeros without the accumulator
+        const int b = acc & 1;
+        if (!wait_bar(&tempty[b], ((acc >> 1) & 1u) ^ 1u, a)) { s_abort = 1; break; }
+        tc_fence_after();
+        const uint32_t dcol = tmem_base + b * 256;
+        bool ok = true;
+        for (int kb = 0; kb < tl.nkb; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!wait_bar(&full[s], (it / STAGES) & 1u, a)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t ad = smem_desc_k128(sA + s * S::kABytes);
+          const uint64_t bd = smem_desc_k128(sB + s * S::kBBytes);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            // advance 16 elements (32 bytes = 2 descriptor units) inside the swizzle row
+            tc_mma(dcol, ad + 2 * k, bd + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+        }
+        if (!ok) { s_abort = 1; break; }
+        tc_commit(&tfull[b]);
+        ++acc;
+      }
+      // every issued MMA has completed before TMEM is released
+      tc_commit(drain);
+      wait_bar(drain, 0, a);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;                    // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;             // accumulator row of this thread
+    uint32_t acc = 0;
+    Tile tl;
+    for (int t = blockIdx.x; tile_of<GROUP_K, BN>(t, a, s_offs, tl); t += gridDim.x) {
+      const int b = acc & 1;
+      const bool have = tl.nkb > 0;
+      if (have) {
+        if (!wait_bar(&tfull[b], (acc >> 1) & 1u, a)) { s_abort = 1; }
+        if (s_abort) break;
+        tc_fence_after();
+      }
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * 256;
+      const int64_t grow = static_cast<int64_t>(tl.m0) + row;
+      if (EPI == kEpiSwiGLU) {
+        // tile = [128 gate columns | 128 up columns] of the interleaved weight layout
+        __nv_bfloat16* hrow = static_cast<__nv_bfloat16*>(a.H) + grow * a.ldh + tl.n0 / 2;
+        __nv_bfloat16* crow = a.C ? static_cast<__nv_bfloat16*>(a.C) + grow * a.ldc + tl.n0 : nullptr;
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(taddr + c, g);
+          tmem_ld32(taddr + BN / 2 + c, u);
+          alignas(16) __nv_bfloat16 hv[32], gv[32], uv[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float gf = __uint_as_float(g[i]), uf = __uint_as_float(u[i]);
+            hv[i] = __float2bfloat16_rn(silu(gf) * uf);
+            gv[i] = __float2bfloat16_rn(gf);
+            uv[i] = __float2bfloat16_rn(uf);
+          }
+#pragma unroll
+          for (int i = 0; i < 4; ++i) reinterpret_cast<int4*>(hrow + c)[i] = reinterpret_cast<int4*>(hv)[i];
+          if (crow) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              reinterpret_cast<int4*>(crow + c)[i] = reinterpret_cast<int4*>(gv)[i];
+              reinterpret_cast<int4*>(crow + BN / 2 + c)[i] = reinterpret_cast<int4*>(uv)[i];
+            }
+          }
+        }
+      } else {
+        const int64_t cbase = GROUP_K ? static_cast<int64_t>(tl.g) * a.c_group_stride : 0;
+        const bool rok = GROUP_K ? (tl.m0 + row < a.M) : true;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t r[32];
+          if (have) {
+            tmem_ld32(taddr + c, r);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = 0u;
+          }
+          const int n = tl.n0 + c;
+          if (!rok || n >= a.N) continue;
+          if (EPI == kEpiF32) {
+            float* crow = static_cast<float*>(a.C) + cbase + grow * a.ldc + n;
+            if (n + 32 <= a.N) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                reinterpret_cast<float4*>(crow)[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                                                 __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+            } else {
+              for (int i = 0; i < a.N - n; ++i) crow[i] = __uint_as_float(r[i]);
+            }
+          } else {
+            __nv_bfloat16* crow = static_cast<__nv_bfloat16*>(a.C) + cbase + grow * a.ldc + n;
+            alignas(16) __nv_bfloat16 v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __float2bfloat16_rn(__uint_as_float(r[i]));
+            if (n + 32 <= a.N) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) reinterpret_cast<int4*>(crow)[i] = reinterpret_cast<int4*>(v)[i];
+            } else {
+              for (int i = 0; i < a.N - n; ++i) crow[i] = v[i];
+            }
+          }
+        }
+      }
+      if (have) {
+        tc_fence_before();
+        mbar_arrive(&tempty[b]);
+        ++acc;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ----------------------------------------------------------------------------- host side
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+EncodeFn encoder() {
+  static EncodeFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    AT_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p != nullptr, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeFn>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 row-major [rows, cols] (row stride ld elements), boxes of box_rows x 64, 128B swizzle.
+CUtensorMap make_map(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", static_cast<int>(r));
+  return m;
+}
+
+template <bool GROUP_K, int BN, int STAGES, int EPI>
+void launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, int grid, cudaStream_t stream) {
+  constexpr size_t smem = 1024 + STAGES * Smem<BN>::kStageBytes + (2 * STAGES + 5) * 8 + 16;
+  auto kfn = grouped_gemm_kernel<GROUP_K, BN, STAGES, EPI>;
+  static bool set = false;
+  if (!set) {
+    AT_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    set = true;
+  }
+  kfn<<<grid, kThreads, smem, stream>>>(ma, mb, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace gemm
+
+// C[rows, N] = A[rows, K] @ B[g]^T per expert segment (offsets on rows, multiples of 128).
+// epilogue: 0 = bf16 C, 1 = fp32 C, 2 = SwiGLU (H = silu(gate) * up, C = pre-activation or none)
+void grouped_gemm_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, const OptTensor& C,
+                    const OptTensor& Hout, int64_t epilogue, at::Tensor error, int64_t num_sms, double timeout_s) {
+  using namespace gemm;
+  const c10::cuda::CUDAGuard guard(A.device());
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "A, B must be bf16");
+  TORCH_CHECK(A.dim() == 2 && A.stride(1) == 1 && B.dim() == 3 && B.is_contiguous(), "A [rows, K], B [G, N, K]");
+  TORCH_CHECK(offsets.scalar_type() == at::kLong && offsets.numel() == B.size(0) + 1 && B.size(0) <= 1024,
+              "offsets must be [G + 1] int64, G <= 1024");
+  Args a{};
+  a.G = static_cast<int>(B.size(0));
+  a.N = static_cast<int>(B.size(1));
+  a.K = static_cast<int>(B.size(2));
+  a.M = static_cast<int>(A.size(0));
+  TORCH_CHECK(A.size(1) == a.K && a.K % 8 == 0, "K mismatch / K % 8");
+  a.offsets = offsets.data_ptr<int64_t>();
+  a.error = reinterpret_cast<uint32_t*>(error.data_ptr<int32_t>());
+  a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
+  const CUtensorMap ma = make_map(A.data_ptr(), A.size(0), a.K, A.stride(0), BM);
+  const CUtensorMap mb = make_map(B.data_ptr(), int64_t(a.G) * a.N, a.K, a.K, 256);
+  if (epilogue == kEpiSwiGLU) {
+    TORCH_CHECK(a.N % 256 == 0 && Hout.has_value(), "SwiGLU needs N % 256 == 0 and an H output");
+    a.H = Hout->data_ptr();
+    a.ldh = Hout->stride(0);
+  }
+  if (C.has_value()) {
+    TORCH_CHECK(C->size(0) >= A.size(0) && C->stride(1) == 1, "C needs at least as many rows as A");
+    a.C = C->data_ptr();
+    a.ldc = C->stride(0);
+    TORCH_CHECK(a.ldc % 8 == 0 && (reinterpret_cast<uintptr_t>(a.C) & 15) == 0, "C rows must be 16-byte aligned");
+  } else {
+    TORCH_CHECK(epilogue == kEpiSwiGLU, "C is required");
+  }
+  const int sms = num_sms > 0 ? static_cast<int>(num_sms) : at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (epilogue == kEpiBF16) launch<false, 256, 4, kEpiBF16>(ma, mb, a, sms, stream);
+  else if (epilogue == kEpiF32) launch<false, 256, 4, kEpiF32>(ma, mb, a, sms, stream);
+  else launch<false, 256, 4, kEpiSwiGLU>(ma, mb, a, sms, stream);
+}
+
+// C[g] (M x N) = A[:, seg_g] @ B[:, seg_g]^T with A [M, tokens], B [N, tokens] (offsets on tokens).
+void grouped_gemm_k(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, at::Tensor C,
+                    at::Tensor error, int64_t num_sms, double timeout_s) {
+  using namespace gemm;
+  const c10::cuda::CUDAGuard guard(A.device());
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "A, B must be bf16");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1, "A [M, tokens], B [N, tokens]");
+  TORCH_CHECK(C.dim() == 3 && C.is_contiguous(), "C must be [G, M, N]");
+  Args a{};
+  a.G = static_cast<int>(C.size(0));
+  a.M = static_cast<int>(A.size(0));
+  a.N = static_cast<int>(B.size(0));
+  TORCH_CHECK(C.size(1) == a.M && C.size(2) == a.N && offsets.numel() == a.G + 1 && a.G <= 1024, "shape mismatch");
+  a.offsets = offsets.data_ptr<int64_t>();
+  a.C = C.data_ptr();
+  a.ldc = a.N;
+  a.c_group_stride = int64_t(a.M) * a.N;
+  a.error = reinterpret_cast<uint32_t*>(error.data_ptr<int32_t>());
+  a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
+  const CUtensorMap ma = make_map(A.data_ptr(), a.M, A.size(1), A.stride(0), BM);
+  const CUtensorMap mb = make_map(B.data_ptr(), a.N, B.size(1), B.stride(0), 256);
+  const int sms = num_sms > 0 ? static_cast<int>(num_sms) : at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (C.scalar_type() == at::kFloat) launch<true, 256, 4, kEpiF32>(ma, mb, a, sms, stream);
+  else launch<true, 256, 4, kEpiBF16>(ma, mb, a, sms, stream);
+}
+
+}  // namespace b200ep

@@ -21,6 +21,8 @@ enum EpochId : int {
   kEpLLD = 2,   // low-latency dispatch (send kernel advances it)
   kEpLLC = 3,   // low-latency combine (send kernel advances it)
   kEpBar = 4,   // device barrier
+  kArLLRecv = 5,  // arrival counter of the low-latency dispatch receive kernel
+  kArLCRecv = 6,  // arrival counter of the low-latency combine receive kernel
   kNumEpochs = 8,
 };
 
@@ -29,6 +31,8 @@ struct Signals {
   uint32_t nd_ready[2][B200EP_MAX_RANKS];   // source s staged its dispatch data for epoch e
   uint32_t nc_ready[2][B200EP_MAX_RANKS];   // rank r delivered all its combine rows for epoch e
   uint64_t ll_hdr[2][B200EP_MAX_RANKS];     // (epoch << 32) | num_tokens of source s
+  uint32_t ll_cnt[2][B200EP_MAX_RANKS];     // cumulative token slots source s has written (per parity)
+  uint32_t lc_cnt[2][B200EP_MAX_RANKS];     // cumulative combine rows rank r has written home
   uint32_t barrier[B200EP_MAX_RANKS];
   uint32_t pad[B200EP_MAX_RANKS];
 };
@@ -39,6 +43,8 @@ struct LocalState {
   uint32_t arrive[kNumEpochs];   // grid-completion counters (reset by the last CTA)
   int64_t nd_recv_off[2][B200EP_MAX_RANKS + 1];   // exclusive prefix of rows per source
   int64_t nd_num_recv[2];
+  uint32_t ll_expect[2][B200EP_MAX_RANKS];        // ll_cnt values already consumed
+  uint32_t lc_expect[2][B200EP_MAX_RANKS];        // lc_cnt values already consumed
 };
 
 struct HeapConfig {
@@ -57,10 +63,10 @@ struct HeapLayout {
   int64_t nd_x[2], nd_topk[2], nd_w[2], nd_lists[2], nd_counts[2], nd_nte[2];
   // normal combine receive (x2): [R][M] rows of 2H bytes, [R][M][K] weights
   int64_t nc_rows[2], nc_w[2];
-  // low-latency dispatch receive (x2): [R][Mll] rows, [R][Mll][K] ids, [R][Mll] flags
-  int64_t ll_rows[2], ll_ids[2], ll_flags[2];
-  // low-latency combine receive (x2): [Mll][K] rows of 2H bytes, [Mll][K] flags
-  int64_t lc_rows[2], lc_flags[2];
+  // low-latency dispatch receive (x2): [R][Mll] rows, [R][Mll][K] ids
+  int64_t ll_rows[2], ll_ids[2];
+  // low-latency combine receive (x2): [Mll][K] rows of 2H bytes
+  int64_t lc_rows[2];
   int64_t total;
 };
 
@@ -92,12 +98,8 @@ inline HeapLayout make_layout(const HeapConfig& c) {
   for (int b = 0; b < 2; ++b) {
     L.ll_rows[b] = take(int64_t(c.R) * c.Mll * L.row_stride);
     L.ll_ids[b] = take(int64_t(c.R) * c.Mll * c.K * 4);
-    L.ll_flags[b] = take(int64_t(c.R) * c.Mll * 4);
   }
-  for (int b = 0; b < 2; ++b) {
-    L.lc_rows[b] = take(int64_t(c.Mll) * c.K * 2LL * c.H);
-    L.lc_flags[b] = take(int64_t(c.Mll) * c.K * 4);
-  }
+  for (int b = 0; b < 2; ++b) L.lc_rows[b] = take(int64_t(c.Mll) * c.K * 2LL * c.H);
   L.total = off;
   return L;
 }

@@ -11,9 +11,20 @@
 // directly into the destination's slot [src][token] of its receive area by
 // 16-byte peer stores; fp8 rows are quantised 1x128 in registers on the way out.
 // Every (src, token) slot of every destination also gets the token's K global
-// expert ids and an epoch flag, so the receiver needs no count exchange: one
-// CTA per local expert walks the slots in (src, token) order, waits on each
-// flag, and compacts the matching rows into recv_x. No host synchronisation.
+// expert ids, so the receiver needs no count exchange: one CTA per local expert
+// walks all slots in (src, token) order and compacts the matching rows into
+// recv_x. No host synchronisation.
+//
+// Completion signalling is batched: each sending CTA adds the number of slots
+// (dispatch) or rows (combine) it wrote to a per-(parity, source) counter in the
+// destination's signal pad with one system-scope fence and one red.release.sys
+// per destination. Counters are cumulative; the receiver keeps what it has
+// already consumed in its local state, so nothing is ever reset. A system-scope
+// fence per row would also order against host-mapped memory and costs far more.
+//
+// Parallelism: CTAs own contiguous token blocks on the send side (16-byte chunks
+// spread over their threads), a CTA per token on the combine receive side with all
+// K slot loads of a chunk issued together.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -21,25 +32,41 @@
 
 namespace b200ep {
 
-constexpr int kLLSendThreads = 256;
+constexpr int kLLThreads = 256;
 constexpr int kLLRecvThreads = 512;
 
 __device__ __forceinline__ uint32_t ldv_u32(const uint32_t* p) { return *reinterpret_cast<const volatile uint32_t*>(p); }
+
+// Last CTA of the grid publishes the new epoch of `which` and resets the arrival counter.
+__device__ __forceinline__ void finish_epoch(LocalState* ls, int which, uint32_t e) {
+  __shared__ int s_last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t prev = atomicAdd(&ls->arrive[which], 1u);
+    s_last = prev == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    ls->arrive[which] = 0;
+    ls->epoch[which] = e;
+  }
+}
 
 // ============================================================================ dispatch send
 struct LLSendArgs {
   HeapView hv;
   const uint8_t* x;   // [T, H] bf16 (or fp16)
   int64_t x_stride;   // bytes
-  int x_fp16;
   const void* topk;
   int topk_i32;
   int T, H, K, E;
   int use_fp8, round_scale;
 };
 
+// grid: CTAs own contiguous blocks of tokens
 template <typename T16>
-__global__ void __launch_bounds__(kLLSendThreads) ll_dispatch_send_kernel(LLSendArgs a) {
+__global__ void __launch_bounds__(kLLThreads) ll_dispatch_send_kernel(LLSendArgs a) {
   const HeapView& hv = a.hv;
   LocalState* ls = hv.local();
   const uint32_t e = ldv_u32(&ls->epoch[kEpLLD]) + 1u;
@@ -47,73 +74,93 @@ __global__ void __launch_bounds__(kLLSendThreads) ll_dispatch_send_kernel(LLSend
   const int me = hv.rank, R = hv.R, Mll = hv.cfg.Mll;
   const int64_t rs = hv.L.row_stride;
   const int H = a.H, K = a.K, EL = a.E / R;
-  const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
-  constexpr int nwarps = kLLSendThreads / 32;
-  __shared__ int s_last;
-
+  const int tid = threadIdx.x;
   const int T = min(a.T, Mll);
+  __shared__ int32_t s_ids[32];
+  __shared__ uint32_t s_mask;
+
   if (blockIdx.x == 0 && tid < R)
     st_release_sys64(&hv.sig(tid)->ll_hdr[slot][me], (static_cast<uint64_t>(e) << 32) | static_cast<uint32_t>(T));
   if (a.T > Mll && blockIdx.x == 0 && tid == 0) report_error(hv.status, kCapacity, 4, me, -1, Mll, a.T);
 
-  for (int t = blockIdx.x * nwarps + warp; t < T; t += gridDim.x * nwarps) {
-    int32_t g = -1;
-    if (lane < K) {
-      const int64_t i = static_cast<int64_t>(t) * K + lane;
-      g = a.topk_i32 ? static_cast<const int32_t*>(a.topk)[i] : static_cast<int32_t>(static_cast<const int64_t*>(a.topk)[i]);
-      if (g >= a.E) g = -1;
+  const int t0 = static_cast<int>(static_cast<int64_t>(T) * blockIdx.x / gridDim.x);
+  const int t1 = static_cast<int>(static_cast<int64_t>(T) * (blockIdx.x + 1) / gridDim.x);
+  for (int t = t0; t < t1; ++t) {
+    if (tid < 32) {
+      int32_t g = -1;
+      if (tid < K) {
+        const int64_t i = static_cast<int64_t>(t) * K + tid;
+        g = a.topk_i32 ? static_cast<const int32_t*>(a.topk)[i]
+                       : static_cast<int32_t>(static_cast<const int64_t*>(a.topk)[i]);
+        if (g >= a.E) g = -1;
+      }
+      s_ids[tid] = g;
+      const uint32_t m = __reduce_or_sync(0xffffffffu, g >= 0 ? (1u << (g / EL)) : 0u);
+      if (tid == 0) s_mask = m;
     }
-    const uint32_t dmask = __reduce_or_sync(0xffffffffu, g >= 0 ? (1u << (g / EL)) : 0u);
+    __syncthreads();
+    const uint32_t dmask = s_mask;
     const int64_t slot_row = static_cast<int64_t>(me) * Mll + t;
     const T16* src = reinterpret_cast<const T16*>(a.x + static_cast<int64_t>(t) * a.x_stride);
+    const int nchunk = H / 8;  // 16-byte chunks of the 16-bit row
     if (!a.use_fp8) {
-      // bf16 rows: each 16-byte chunk is loaded once and stored to every destination
-      for (int c = lane * 8; c < H; c += 256) {
-        const int4 v = *reinterpret_cast<const int4*>(src + c);
+      for (int j0 = tid; j0 < nchunk; j0 += 4 * kLLThreads) {
+        int4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = j0 + u * kLLThreads;
+          if (j < nchunk) v[u] = reinterpret_cast<const int4*>(src)[j];
+        }
         for (uint32_t m = dmask; m; m &= m - 1) {
           const int p = __ffs(m) - 1;
-          *reinterpret_cast<int4*>(hv.base[p] + hv.L.ll_rows[slot] + slot_row * rs + c * 2) = v;
+          int4* dst = reinterpret_cast<int4*>(hv.base[p] + hv.L.ll_rows[slot] + slot_row * rs);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int j = j0 + u * kLLThreads;
+            if (j < nchunk) dst[j] = v[u];
+          }
         }
       }
     } else {
-      for (int c = 0; c < H; c += 256) {
-        const int off = c + lane * 8;
-        const bool act = off < H;
-        float v[8];
-        load8(v, src + off, act);
-        const Quant8 qr = quant8_e4m3(v, a.round_scale);
+      // a half-warp quantises one 128-element block; every thread runs the same number of
+      // iterations so the shuffles inside quant8_e4m3 always see full warps
+      const int iters = (nchunk + kLLThreads - 1) / kLLThreads;
+      for (int it0 = 0; it0 < iters; it0 += 4) {
+        float vv[4][8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = (it0 + u) * kLLThreads + tid;
+          load8(vv[u], src + static_cast<int64_t>(j) * 8, it0 + u < iters && j < nchunk);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+        if (it0 + u >= iters) break;
+        const int j = (it0 + u) * kLLThreads + tid;
+        const bool act = j < nchunk;
+        const Quant8 qr = quant8_e4m3(vv[u], a.round_scale);
         if (act) {
-          const uint2 q = qr.q;
-          const float scale = qr.scale;
           for (uint32_t m = dmask; m; m &= m - 1) {
             const int p = __ffs(m) - 1;
             uint8_t* row = hv.base[p] + hv.L.ll_rows[slot] + slot_row * rs;
-            *reinterpret_cast<uint2*>(row + off) = q;
-            if ((lane & 15) == 0) reinterpret_cast<float*>(row + H)[off / 128] = scale;
+            *reinterpret_cast<uint2*>(row + j * 8) = qr.q;
+            if ((tid & 15) == 0) reinterpret_cast<float*>(row + H)[j / 16] = qr.scale;
           }
+        }
         }
       }
     }
     // ids go to every rank (a non-routed rank learns that it is not a destination)
-    if (lane < K)
-      for (int p = 0; p < R; ++p) hv.at<int32_t>(p, hv.L.ll_ids[slot])[slot_row * K + lane] = g;
-    __syncwarp();
-    if (lane < R) {
-      fence_sys();
-      st_release_sys(hv.at<uint32_t>(lane, hv.L.ll_flags[slot]) + slot_row, e);
+    for (int i = tid; i < R * K; i += kLLThreads) {
+      const int p = i / K, k = i % K;
+      hv.at<int32_t>(p, hv.L.ll_ids[slot])[slot_row * K + k] = s_ids[k];
     }
+    __syncthreads();
   }
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    const uint32_t prev = atomicAdd(&ls->arrive[kEpLLD], 1u);
-    s_last = prev == gridDim.x - 1;
+  if (tid < R && t1 > t0) {
+    fence_sys();
+    red_add_release_sys(&hv.sig(tid)->ll_cnt[slot][me], static_cast<uint32_t>(t1 - t0));
   }
-  __syncthreads();
-  if (s_last && tid == 0) {
-    ls->arrive[kEpLLD] = 0;
-    ls->epoch[kEpLLD] = e;
-  }
+  finish_epoch(ls, kEpLLD, e);
 }
 
 void ll_dispatch_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& topk_idx, int64_t num_experts,
@@ -126,7 +173,6 @@ void ll_dispatch_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& top
   a.hv = hv;
   a.x = static_cast<const uint8_t*>(x.data_ptr());
   a.x_stride = x.stride(0) * 2;
-  a.x_fp16 = x.scalar_type() == at::kHalf;
   a.topk = topk_idx.data_ptr();
   a.topk_i32 = topk_idx.scalar_type() == at::kInt;
   a.T = static_cast<int>(x.size(0));
@@ -138,15 +184,15 @@ void ll_dispatch_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& top
   TORCH_CHECK(a.H % 8 == 0 && a.H <= hv.cfg.H, "low-latency hidden must be a multiple of 8 within the buffer");
   TORCH_CHECK(!use_fp8 || a.H % 128 == 0, "fp8 needs hidden % 128 == 0");
   TORCH_CHECK(a.K <= 32 && a.K <= hv.cfg.K && a.E <= hv.cfg.E && a.E % hv.R == 0, "bad top-k / experts");
-  TORCH_CHECK((a.x_stride % 16) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0, "x rows must be 16-byte aligned");
-  const int warps_needed = std::max(1, (std::min(a.T, hv.cfg.Mll) + 7) / 8);
-  int grid = num_sms > 0 ? static_cast<int>(num_sms) : heap.num_sms();
-  grid = std::max(1, std::min(grid, warps_needed));
+  TORCH_CHECK(a.T == 0 || ((a.x_stride % 16) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0),
+              "x rows must be 16-byte aligned");
+  const int sms = num_sms > 0 ? static_cast<int>(num_sms) : heap.num_sms();
+  const int grid = std::max(1, std::min(std::min(a.T, hv.cfg.Mll), 2 * sms));
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (a.x_fp16)
-    ll_dispatch_send_kernel<__half><<<grid, kLLSendThreads, 0, stream>>>(a);
+  if (x.scalar_type() == at::kHalf)
+    ll_dispatch_send_kernel<__half><<<grid, kLLThreads, 0, stream>>>(a);
   else
-    ll_dispatch_send_kernel<__nv_bfloat16><<<grid, kLLSendThreads, 0, stream>>>(a);
+    ll_dispatch_send_kernel<__nv_bfloat16><<<grid, kLLThreads, 0, stream>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -165,6 +211,8 @@ struct LLRecvArgs {
   int use_fp8, ue8m0;
 };
 
+// grid: one CTA per local expert. One pass over the (src, token) slots of all
+// sources flattened in (src, token) order, 512 slots per tile.
 __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecvArgs a) {
   const HeapView& hv = a.hv;
   LocalState* ls = hv.local();
@@ -181,98 +229,140 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
   const int64_t PB = a.use_fp8 ? H : 2LL * H;   // payload bytes
   const int nsb = H / 128;                      // scale blocks
 
-  __shared__ int s_T, s_fail;
+  __shared__ int s_T[B200EP_MAX_RANKS];
+  __shared__ int s_toff[B200EP_MAX_RANKS + 1];   // prefix of T over sources
+  __shared__ int s_bcnt[B200EP_MAX_RANKS];       // rows of this expert per source
+  __shared__ int s_fail, s_tile_total;
   __shared__ int s_wcnt[nwarps];
   __shared__ int s_tok[kLLRecvThreads];
+  __shared__ int s_src[kLLRecvThreads];
   __shared__ int s_dst[kLLRecvThreads];
-  int running = 0;
   if (tid == 0) s_fail = 0;
-  for (int s = 0; s < R; ++s) {
+  __syncthreads();
+  // headers: one thread per source
+  if (tid < R) {
+    const uint64_t* hdr = &hv.sig(me)->ll_hdr[slot][tid];
+    const uint64_t t0 = global_ns();
+    uint64_t v = ld_acquire_sys64(hdr);
+    uint32_t spins = 0;
+    while (!epoch_reached(static_cast<uint32_t>(v >> 32), e)) {
+      if ((++spins & 63u) == 0u && (global_ns() - t0 > hv.timeout_ns || has_error(hv.status))) {
+        report_error(hv.status, kTimeoutLLHeader, 5, me, tid, e, static_cast<uint32_t>(v >> 32));
+        s_fail = 1;
+        break;
+      }
+      v = ld_acquire_sys64(hdr);
+    }
+    s_T[tid] = epoch_reached(static_cast<uint32_t>(v >> 32), e) ? static_cast<int>(v & 0xffffffffu) : 0;
+    s_bcnt[tid] = 0;
+    // every slot of source tid has landed once its counter passes what was consumed before
+    if (!s_fail && s_T[tid] > 0) {
+      const uint32_t target = ls->ll_expect[slot][tid] + static_cast<uint32_t>(s_T[tid]);
+      if (!wait_epoch(&hv.sig(me)->ll_cnt[slot][tid], target, hv.timeout_ns, hv.status, kTimeoutLLRow, 5, me, tid))
+        s_fail = 1;
+    }
+    if (a.wait_stats && le == 0)
+      atomicAdd(reinterpret_cast<unsigned long long*>(&a.wait_stats[tid]),
+                static_cast<unsigned long long>(global_ns() - t0));
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0;
+    for (int s = 0; s < R; ++s) {
+      s_toff[s] = run;
+      run += min(s_T[s], Mll);
+    }
+    s_toff[R] = run;
+  }
+  __syncthreads();
+  const int total = s_toff[R];
+  int running = 0;
+  for (int tile = 0; tile < total; tile += kLLRecvThreads) {
+    const int i = tile + tid;
+    int hit = -1, s = 0, t = 0;
+    if (i < total && !s_fail) {
+      while (s + 1 < R && s_toff[s + 1] <= i) ++s;
+      t = i - s_toff[s];
+      const int64_t slot_row = static_cast<int64_t>(s) * Mll + t;
+      const int32_t* ids = hv.at<int32_t>(me, hv.L.ll_ids[slot]) + slot_row * K;
+      if ((K & 3) == 0) {
+        // the counter acquire above ordered these loads; vector loads keep the chain short
+        for (int k0 = 0; k0 < K && hit < 0; k0 += 4) {
+          const int4 v = *reinterpret_cast<const int4*>(ids + k0);
+          if (v.x == want) hit = k0;
+          else if (v.y == want) hit = k0 + 1;
+          else if (v.z == want) hit = k0 + 2;
+          else if (v.w == want) hit = k0 + 3;
+        }
+      } else {
+        for (int k = 0; k < K; ++k)
+          if (hit < 0 && ids[k] == want) hit = k;
+      }
+    }
+    const uint32_t b = __ballot_sync(0xffffffffu, hit >= 0);
+    if (lane == 0) s_wcnt[warp] = __popc(b);
+    __syncthreads();
     if (tid == 0) {
-      const uint64_t* hdr = &hv.sig(me)->ll_hdr[slot][s];
-      uint64_t v = ld_acquire_sys64(hdr);
-      const uint64_t t0 = global_ns();
-      uint32_t spins = 0;
-      while (!epoch_reached(static_cast<uint32_t>(v >> 32), e)) {
-        if ((++spins & 63u) == 0u && (global_ns() - t0 > hv.timeout_ns || has_error(hv.status))) {
-          report_error(hv.status, kTimeoutLLHeader, 5, me, s, e, static_cast<uint32_t>(v >> 32));
-          s_fail = 1;
-          break;
-        }
-        v = ld_acquire_sys64(hdr);
+      int run = 0;
+      for (int w = 0; w < nwarps; ++w) {
+        const int c = s_wcnt[w];
+        s_wcnt[w] = run;
+        run += c;
       }
-      s_T = s_fail ? 0 : static_cast<int>(v & 0xffffffffu);
-      if (a.wait_stats && le == 0) atomicAdd(reinterpret_cast<unsigned long long*>(&a.wait_stats[s]),
-                                             static_cast<unsigned long long>(global_ns() - t0));
+      s_tile_total = run;
     }
     __syncthreads();
-    const int Ts = s_T;
-    const int start = running;
-    for (int tile = 0; tile < Ts; tile += kLLRecvThreads) {
-      const int t = tile + tid;
-      int hit = -1;
-      if (t < Ts && !s_fail) {
-        const int64_t slot_row = static_cast<int64_t>(s) * Mll + t;
-        if (wait_epoch(hv.at<uint32_t>(me, hv.L.ll_flags[slot]) + slot_row, e, hv.timeout_ns, hv.status,
-                       kTimeoutLLRow, 5, me, s)) {
-          const int32_t* ids = hv.at<int32_t>(me, hv.L.ll_ids[slot]) + slot_row * K;
-          for (int k = 0; k < K; ++k)
-            if (hit < 0 && *reinterpret_cast<const volatile int32_t*>(ids + k) == want) hit = k;
+    const int tile_total = s_tile_total;
+    if (hit >= 0) {
+      const int q = s_wcnt[warp] + __popc(b & lanemask_lt());
+      const int p = running + q;
+      s_tok[q] = t;
+      s_src[q] = s;
+      s_dst[q] = p;
+      a.src_info[le * RM + p] = t;
+      a.pair_meta[le * RM + p] = s * K + hit;
+      atomicAdd(&s_bcnt[s], 1);
+    }
+    __syncthreads();  // rows acquired by other threads are ordered by the barrier
+    for (int q = warp; q < tile_total; q += nwarps) {
+      const int t2 = s_tok[q], s2 = s_src[q], p = s_dst[q];
+      const uint8_t* row = hv.at<uint8_t>(me, hv.L.ll_rows[slot]) + (static_cast<int64_t>(s2) * Mll + t2) * rs;
+      const int64_t o = le * RM + p;
+      warp_copy(a.recv_x + o * PB, row, PB);
+      if (a.use_fp8) {
+        const float* sc = reinterpret_cast<const float*>(row + H);
+        if (a.ue8m0) {
+          for (int j = lane; j < nsb; j += 32)
+            a.recv_scales[o * nsb + j] = static_cast<uint8_t>((__float_as_uint(sc[j]) >> 23) & 0xFFu);
         } else {
-          s_fail = 1;
+          warp_copy(a.recv_scales + o * nsb * 4, sc, nsb * 4LL);
         }
       }
-      const uint32_t b = __ballot_sync(0xffffffffu, hit >= 0);
-      if (lane == 0) s_wcnt[warp] = __popc(b);
-      __syncthreads();
-      if (tid == 0) {
-        int run = 0;
-        for (int w = 0; w < nwarps; ++w) {
-          const int c = s_wcnt[w];
-          s_wcnt[w] = run;
-          run += c;
-        }
-        s_T = run;  // reuse as the tile total
-      }
-      __syncthreads();
-      const int tile_total = s_T;
-      if (hit >= 0) {
-        const int q = s_wcnt[warp] + __popc(b & lanemask_lt());
-        const int p = running + q;
-        s_tok[q] = t;
-        s_dst[q] = p;
-        a.src_info[le * RM + p] = t;
-        a.pair_meta[le * RM + p] = s * K + hit;
-      }
-      __syncthreads();
-      fence_sys();
-      for (int q = warp; q < tile_total; q += nwarps) {
-        const int t2 = s_tok[q], p = s_dst[q];
-        const uint8_t* row = hv.at<uint8_t>(me, hv.L.ll_rows[slot]) + (static_cast<int64_t>(s) * Mll + t2) * rs;
-        const int64_t o = le * RM + p;
-        warp_copy(a.recv_x + o * PB, row, PB);
-        if (a.use_fp8) {
-          const float* sc = reinterpret_cast<const float*>(row + H);
-          if (a.ue8m0) {
-            for (int i = lane; i < nsb; i += 32)
-              a.recv_scales[o * nsb + i] = static_cast<uint8_t>((__float_as_uint(sc[i]) >> 23) & 0xFFu);
-          } else {
-            warp_copy(a.recv_scales + o * nsb * 4, sc, nsb * 4LL);
-          }
-        }
-      }
-      running += tile_total;
-      __syncthreads();
-      if (tid == 0) s_T = Ts;
-      __syncthreads();
     }
-    if (tid == 0) a.layout_range[le * R + s] = (static_cast<int64_t>(start) << 32) | static_cast<int64_t>(running - start);
+    running += tile_total;
     __syncthreads();
+  }
+  if (tid < R) {
+    int start = 0;
+    for (int s = 0; s < tid; ++s) start += s_bcnt[s];
+    a.layout_range[le * R + tid] = (static_cast<int64_t>(start) << 32) | static_cast<int64_t>(s_bcnt[tid]);
   }
   for (int64_t p = running + tid; p < RM; p += kLLRecvThreads) a.src_info[le * RM + p] = -1;
   if (tid == 0) {
     a.recv_count[le] = running;
     if (a.cum_stats) atomicAdd(&a.cum_stats[le], running);
+  }
+  // the last expert CTA records the slots consumed from each source
+  __shared__ int s_last;
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(&ls->arrive[kArLLRecv], 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last) {
+    if (tid < R) ls->ll_expect[slot][tid] += static_cast<uint32_t>(s_T[tid]);
+    if (tid == 0) ls->arrive[kArLLRecv] = 0;
   }
 }
 
@@ -308,16 +398,17 @@ void ll_dispatch_recv(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_s
 // ============================================================================ combine send
 struct LCSendArgs {
   HeapView hv;
-  const uint8_t* x;     // [EL, R*Mll, H] 16-bit
+  const uint8_t* x;     // [EL, >= R*Mll rows, H] 16-bit
   int64_t x_row_stride; // bytes between rows
   int64_t x_exp_stride; // bytes between experts
   const int32_t* recv_count;
   const int32_t* src_info;
   const int32_t* pair_meta;
-  int H, K, EL, cta_per_expert;
+  int H, K, EL;
 };
 
-__global__ void __launch_bounds__(kLLSendThreads) ll_combine_send_kernel(LCSendArgs a) {
+// persistent grid over (expert, row) items; a CTA copies one row home and flags it
+__global__ void __launch_bounds__(kLLThreads) ll_combine_send_kernel(LCSendArgs a) {
   const HeapView& hv = a.hv;
   LocalState* ls = hv.local();
   const uint32_t e = ldv_u32(&ls->epoch[kEpLLC]) + 1u;
@@ -325,42 +416,50 @@ __global__ void __launch_bounds__(kLLSendThreads) ll_combine_send_kernel(LCSendA
   const int R = hv.R, Mll = hv.cfg.Mll, H = a.H, K = a.K;
   const int64_t RM = static_cast<int64_t>(R) * Mll;
   const int64_t RB = 2LL * H;
+  __shared__ uint32_t s_n[B200EP_MAX_RANKS];
+  __shared__ int s_cnt[1025];   // prefix of the per-expert row counts
   const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
-  constexpr int nwarps = kLLSendThreads / 32;
-  __shared__ int s_last;
-  const int le = blockIdx.x / a.cta_per_expert, sub = blockIdx.x % a.cta_per_expert;
-  const int count = static_cast<int>(a.recv_count[le] < RM ? a.recv_count[le] : RM);
-  for (int p = sub * nwarps + warp; p < count; p += a.cta_per_expert * nwarps) {
+  constexpr int nwarps = kLLThreads / 32;
+  if (tid < R) s_n[tid] = 0;
+  if (tid == 0) {
+    int run = 0;
+    for (int le = 0; le < a.EL; ++le) {
+      s_cnt[le] = run;
+      run += min(a.recv_count[le], static_cast<int>(RM));
+    }
+    s_cnt[a.EL] = run;
+  }
+  __syncthreads();
+  const int total = s_cnt[a.EL];
+  // valid rows only, one warp per row
+  for (int i = blockIdx.x * nwarps + warp; i < total; i += gridDim.x * nwarps) {
+    int lo = 0, hi = a.EL - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_cnt[mid] <= i) lo = mid; else hi = mid - 1;
+    }
+    const int le = lo, p = i - s_cnt[le];
     const int t = a.src_info[le * RM + p];
     const int sk = a.pair_meta[le * RM + p];
     const int s = sk / K, k = sk % K;
     if (t < 0 || t >= Mll || s < 0 || s >= R) continue;
     uint8_t* dst = hv.base[s] + hv.L.lc_rows[slot] + (static_cast<int64_t>(t) * K + k) * RB;
     warp_copy(dst, a.x + le * a.x_exp_stride + p * a.x_row_stride, RB);
-    __syncwarp();
-    if (lane == 0) {
-      fence_sys();
-      st_release_sys(hv.at<uint32_t>(s, hv.L.lc_flags[slot]) + static_cast<int64_t>(t) * K + k, e);
-    }
+    if (lane == 0) atomicAdd(&s_n[s], 1u);
   }
   __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    const uint32_t prev = atomicAdd(&ls->arrive[kEpLLC], 1u);
-    s_last = prev == gridDim.x - 1;
+  if (tid < R && s_n[tid] > 0) {
+    fence_sys();
+    red_add_release_sys(&hv.sig(tid)->lc_cnt[slot][hv.rank], s_n[tid]);
   }
-  __syncthreads();
-  if (s_last && tid == 0) {
-    ls->arrive[kEpLLC] = 0;
-    ls->epoch[kEpLLC] = e;
-  }
+  finish_epoch(ls, kEpLLC, e);
 }
 
 void ll_combine_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& recv_count, const at::Tensor& src_info,
                      const at::Tensor& pair_meta, int64_t num_experts, int64_t num_sms) {
   const c10::cuda::CUDAGuard guard(x.device());
   HeapView hv = heap.view();
-  TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1 && x.element_size() == 2, "x must be 16-bit [EL, R*M, H]");
+  TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1 && x.element_size() == 2, "x must be 16-bit [EL, rows, H]");
   LCSendArgs a{};
   a.hv = hv;
   a.x = static_cast<const uint8_t*>(x.data_ptr());
@@ -372,12 +471,11 @@ void ll_combine_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& recv
   a.H = static_cast<int>(x.size(2));
   a.K = hv.cfg.K;
   a.EL = static_cast<int>(num_experts / hv.R);
-  TORCH_CHECK(x.size(0) == a.EL && x.size(1) == int64_t(hv.R) * hv.cfg.Mll, "x shape must be [EL, R*M, H]");
+  TORCH_CHECK(x.size(0) == a.EL && a.EL <= 1024, "x must have one slab per local expert (at most 1024)");
   TORCH_CHECK(a.H % 8 == 0 && a.x_row_stride % 16 == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0,
               "x rows must be 16-byte aligned");
   const int sms = num_sms > 0 ? static_cast<int>(num_sms) : heap.num_sms();
-  a.cta_per_expert = std::max(1, (2 * sms) / std::max(1, a.EL));
-  ll_combine_send_kernel<<<a.EL * a.cta_per_expert, kLLSendThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  ll_combine_send_kernel<<<sms, kLLThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -391,52 +489,99 @@ struct LCRecvArgs {
   int T, H, K, E;
 };
 
+// grid: one CTA per token; every thread issues the K slot loads of a 16-byte chunk together
 template <typename T16>
-__global__ void __launch_bounds__(kLLSendThreads) ll_combine_recv_kernel(LCRecvArgs a) {
+__global__ void __launch_bounds__(kLLThreads) ll_combine_recv_kernel(LCRecvArgs a) {
   const HeapView& hv = a.hv;
   LocalState* ls = hv.local();
   const uint32_t e = ldv_u32(&ls->epoch[kEpLLC]);
   const int slot = e & 1u;
   const int me = hv.rank, H = a.H, K = a.K;
   const int64_t RB = 2LL * H;
-  const int lane = lane_id(), warp = warp_id();
-  constexpr int nwarps = kLLSendThreads / 32;
-  __shared__ float s_w[nwarps][32];
+  const int tid = threadIdx.x;
+  __shared__ float s_w[32];
+  __shared__ uint32_t s_valid;
+  __shared__ uint32_t s_exp[B200EP_MAX_RANKS];
+  __shared__ int s_fail;
+  const int R = hv.R, EL = a.E / R;
   const uint8_t* rows = hv.at<uint8_t>(me, hv.L.lc_rows[slot]);
-  for (int t = blockIdx.x * nwarps + warp; t < a.T; t += gridDim.x * nwarps) {
-    float wk = 0.f;
-    bool valid = false;
-    if (lane < K) {
-      const int64_t i = static_cast<int64_t>(t) * K + lane;
-      const int64_t g = a.topk_i32 ? static_cast<const int32_t*>(a.topk)[i] : static_cast<const int64_t*>(a.topk)[i];
-      valid = g >= 0 && g < a.E;
-      wk = valid ? a.w[i] : 0.f;
-      if (valid && !wait_epoch(hv.at<uint32_t>(me, hv.L.lc_flags[slot]) + i, e, hv.timeout_ns, hv.status,
-                               kTimeoutLLCombine, 6, me, -1))
-        valid = false;
+  // rows expected from every rank = this rank's valid (token, k) entries owned by it
+  if (tid < R) s_exp[tid] = 0;
+  if (tid == 0) s_fail = 0;
+  __syncthreads();
+  for (int64_t i = tid; i < static_cast<int64_t>(a.T) * K; i += kLLThreads) {
+    const int64_t g = a.topk_i32 ? static_cast<const int32_t*>(a.topk)[i] : static_cast<const int64_t*>(a.topk)[i];
+    if (g >= 0 && g < a.E) atomicAdd(&s_exp[g / EL], 1u);
+  }
+  __syncthreads();
+  if (tid < R && s_exp[tid] > 0) {
+    const uint32_t target = ls->lc_expect[slot][tid] + s_exp[tid];
+    if (!wait_epoch(&hv.sig(me)->lc_cnt[slot][tid], target, hv.timeout_ns, hv.status, kTimeoutLLCombine, 6, me, tid))
+      s_fail = 1;
+  }
+  __syncthreads();  // rows acquired by threads < R are read by every thread after this
+  for (int t = blockIdx.x; t < a.T && !s_fail; t += gridDim.x) {
+    if (tid < 32) {
+      bool valid = false;
+      float wk = 0.f;
+      if (tid < K) {
+        const int64_t i = static_cast<int64_t>(t) * K + tid;
+        const int64_t g = a.topk_i32 ? static_cast<const int32_t*>(a.topk)[i] : static_cast<const int64_t*>(a.topk)[i];
+        valid = g >= 0 && g < a.E;
+        wk = valid ? a.w[i] : 0.f;
+      }
+      s_w[tid] = wk;
+      const uint32_t vm = __ballot_sync(0xffffffffu, valid);
+      if (tid == 0) s_valid = vm;
     }
-    s_w[warp][lane] = valid ? wk : 0.f;
-    const uint32_t vmask = __ballot_sync(0xffffffffu, valid);
-    __syncwarp();
-    fence_sys();
+    __syncthreads();
+    const uint32_t vmask = s_valid;
+    const uint8_t* trow = rows + static_cast<int64_t>(t) * K * RB;
     T16* out = reinterpret_cast<T16*>(a.out) + static_cast<int64_t>(t) * H;
-    for (int c = lane * 8; c < H; c += 256) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (uint32_t m = vmask; m; m &= m - 1) {
-        const int k = __ffs(m) - 1;
-        const float wv = s_w[warp][k];
-        const int4 raw = *reinterpret_cast<const int4*>(rows + (static_cast<int64_t>(t) * K + k) * RB + c * 2);
-        const T16* h = reinterpret_cast<const T16*>(&raw);
+    const int nchunk = H / 8;
+    for (int j = tid; j < nchunk; j += kLLThreads) {
+      int4 v[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] += static_cast<float>(h[i]) * wv;
+      for (int k = 0; k < 8; ++k)
+        if (k < K && ((vmask >> k) & 1u)) v[k] = reinterpret_cast<const int4*>(trow + k * RB)[j];
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (k < K && ((vmask >> k) & 1u)) {
+          const float wv = s_w[k];
+          const T16* h = reinterpret_cast<const T16*>(&v[k]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] += static_cast<float>(h[i]) * wv;
+        }
+      }
+      for (int k = 8; k < K; ++k) {  // top-k above 8: remaining slots one at a time
+        if ((vmask >> k) & 1u) {
+          const int4 r = reinterpret_cast<const int4*>(trow + k * RB)[j];
+          const float wv = s_w[k];
+          const T16* h = reinterpret_cast<const T16*>(&r);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] += static_cast<float>(h[i]) * wv;
+        }
       }
       int4 o;
       T16* oh = reinterpret_cast<T16*>(&o);
 #pragma unroll
       for (int i = 0; i < 8; ++i) oh[i] = static_cast<T16>(acc[i]);
-      *reinterpret_cast<int4*>(out + c) = o;
+      reinterpret_cast<int4*>(out)[j] = o;
     }
-    __syncwarp();
+    __syncthreads();
+  }
+  // the last CTA records the rows consumed from each rank
+  __shared__ int s_last;
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(&ls->arrive[kArLCRecv], 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last) {
+    if (tid < R) ls->lc_expect[slot][tid] += s_exp[tid];
+    if (tid == 0) ls->arrive[kArLCRecv] = 0;
   }
 }
 
@@ -457,14 +602,13 @@ void ll_combine_recv(SymmHeap& heap, const at::Tensor& topk_idx, const at::Tenso
   a.H = static_cast<int>(out.size(1));
   a.K = static_cast<int>(topk_idx.size(1));
   a.E = hv.cfg.E;
-  TORCH_CHECK(a.H % 8 == 0 && a.T <= hv.cfg.Mll && a.K <= hv.cfg.K, "combine shape exceeds the buffer");
-  constexpr int nwarps = kLLSendThreads / 32;
-  int grid = std::max(1, (a.T + nwarps - 1) / nwarps);
+  TORCH_CHECK(a.H % 8 == 0 && a.T <= hv.cfg.Mll && a.K <= hv.cfg.K && a.K <= 32, "combine shape exceeds the buffer");
+  if (a.T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   if (out.scalar_type() == at::kHalf)
-    ll_combine_recv_kernel<__half><<<grid, kLLSendThreads, 0, stream>>>(a);
+    ll_combine_recv_kernel<__half><<<a.T, kLLThreads, 0, stream>>>(a);
   else
-    ll_combine_recv_kernel<__nv_bfloat16><<<grid, kLLSendThreads, 0, stream>>>(a);
+    ll_combine_recv_kernel<__nv_bfloat16><<<a.T, kLLThreads, 0, stream>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   (void)num_sms;
 }

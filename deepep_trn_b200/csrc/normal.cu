@@ -48,14 +48,17 @@ struct NdPrepArgs {
   int mode;              // 0: 16-bit payload, 1: fp8 payload + scales given, 2: quantise 16-bit -> fp8
   int x_fp16;
   int round_scale;
-  const void* topk;
+  const void* topk;       // [T, K] or null (cached dispatch)
   int topk_i32;
   const float* topk_w;
+  const int32_t* nte;     // caller's num_tokens_per_expert [E]
+  int has_nte;            // explicit: an empty topk tensor may have a null pointer
   const bool* in_rank;
   int32_t* token_pos;    // [T, R]
   int64_t* recv_off;     // [R + 1] copy for the handle
   int T, H, K, E;
   uint64_t ticket;
+  int local_direct;      // the receiver reads its own rows from x directly: stage only rows peers need
 };
 
 __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) {
@@ -73,7 +76,6 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
 
   __shared__ int32_t s_cnt[B200EP_MAX_RANKS][kPrepThreads / 32];
   __shared__ int32_t s_base[B200EP_MAX_RANKS];
-  __shared__ int32_t s_nte[kPrepMaxExperts];
   __shared__ int s_last, s_fail;
   const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
   constexpr int nwarps = kPrepThreads / 32;
@@ -85,9 +87,6 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
   // ---------------------------------------------------------------- CTA 0: scan + expert counts
   if (blockIdx.x == 0) {
     if (tid < B200EP_MAX_RANKS) s_base[tid] = 0;
-    const bool do_nte = a.topk != nullptr;
-    if (do_nte)
-      for (int i = tid; i < a.E; i += kPrepThreads) s_nte[i] = 0;
     __syncthreads();
     for (int tile = 0; tile < T; tile += kPrepThreads) {
       const int t = tile + tid;
@@ -95,13 +94,6 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
       if (t < T && t < M) {
         const bool* row = a.in_rank + static_cast<int64_t>(t) * R;
         for (int r = 0; r < R; ++r) mask |= (row[r] ? 1u : 0u) << r;
-        if (do_nte) {
-          for (int k = 0; k < K; ++k) {
-            const int64_t i = static_cast<int64_t>(t) * K + k;
-            const int64_t g = a.topk_i32 ? static_cast<const int32_t*>(a.topk)[i] : static_cast<const int64_t*>(a.topk)[i];
-            if (g >= 0 && g < a.E) atomicAdd(&s_nte[g], 1);
-          }
-        }
       }
       uint32_t bal[B200EP_MAX_RANKS];
 #pragma unroll
@@ -142,8 +134,8 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
     int32_t* stage_counts = hv.at<int32_t>(me, hv.L.nd_counts[slot]);
     int32_t* stage_nte = hv.at<int32_t>(me, hv.L.nd_nte[slot]);
     if (tid < R) stage_counts[tid] = s_base[tid];
-    if (do_nte)
-      for (int i = tid; i < a.E; i += kPrepThreads) stage_nte[i] = s_nte[i];
+    if (a.has_nte)
+      for (int i = tid; i < a.E; i += kPrepThreads) stage_nte[i] = a.nte[i];
   }
 
   // ---------------------------------------------------------------- copiers: stage rows + top-k
@@ -155,7 +147,14 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
     for (int t = gw; t < Tc; t += GW) {
       uint8_t* dst = stage_x + static_cast<int64_t>(t) * rs;
       const uint8_t* src = a.x + static_cast<int64_t>(t) * a.x_stride;
-      if (a.mode == 0) {
+      bool stage = true;
+      if (a.local_direct) {
+        const bool peer = lane < R && lane != me && a.in_rank[static_cast<int64_t>(t) * R + lane];
+        stage = __any_sync(0xffffffffu, peer);
+      }
+      if (!stage) {
+        // only this rank receives the token: the pull reads it from x
+      } else if (a.mode == 0) {
         warp_copy(dst, src, 2LL * H);
       } else if (a.mode == 1) {
         warp_copy(dst, src, H);
@@ -177,9 +176,11 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
   }
 
   // ---------------------------------------------------------------- grid completion
+  // staging is local memory that peers read after the last CTA's system-scope release,
+  // so a GPU-scope fence before the arrival is enough here
   __syncthreads();
   if (tid == 0) {
-    __threadfence_system();
+    __threadfence();
     const uint32_t prev = atomicAdd(&ls->arrive[kEpND], 1u);
     s_last = (prev == gridDim.x - 1);
     s_fail = 0;
@@ -188,14 +189,15 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
   if (!s_last) return;
 
   // ---------------------------------------------------------------- last CTA: notify
-  fence_sys();
-  if (tid < R) st_release_sys(&hv.sig(tid)->nd_ready[slot][me], e);
+  if (tid < R) {
+    fence_sys();  // acquire side of the arrival counter, then release to the peer
+    st_release_sys(&hv.sig(tid)->nd_ready[slot][me], e);
+  }
   if (tid < R) {
     if (!wait_epoch(&hv.sig(me)->nd_ready[slot][tid], e, hv.timeout_ns, hv.status, kTimeoutReady, 1, me, tid))
       atomicExch(&s_fail, 1);
   }
   __syncthreads();
-  fence_sys();
   __shared__ int32_t s_rc[B200EP_MAX_RANKS];
   if (tid < R) {
     int32_t c = s_fail ? 0 : ld_volatile_i32(hv.at<int32_t>(tid, hv.L.nd_counts[slot]) + me);
@@ -221,7 +223,7 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
     host->notify.num_recv = off;
   }
   const int EL = a.E / R;
-  if (a.topk) {
+  if (a.has_nte) {
     for (int le = tid; le < EL && le < 1024; le += kPrepThreads) {
       int32_t sum = 0;
       if (!s_fail)
@@ -239,8 +241,8 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
 }
 
 void nd_prepare(SymmHeap& heap, const at::Tensor& x, const OptTensor& x_scales, int64_t mode, bool round_scale,
-                const OptTensor& topk_idx, const OptTensor& topk_w, const at::Tensor& in_rank, at::Tensor token_pos,
-                at::Tensor recv_off, int64_t num_experts, int64_t ticket, int64_t num_sms) {
+                const OptTensor& topk_idx, const OptTensor& topk_w, const OptTensor& nte, const at::Tensor& in_rank,
+                at::Tensor token_pos, at::Tensor recv_off, int64_t num_experts, int64_t ticket, int64_t num_sms) {
   const c10::cuda::CUDAGuard guard(x.device());
   HeapView hv = heap.view();
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be [T, H] with unit inner stride");
@@ -285,11 +287,19 @@ void nd_prepare(SymmHeap& heap, const at::Tensor& x, const OptTensor& x_scales, 
     TORCH_CHECK(topk_w->is_contiguous() && topk_w->scalar_type() == at::kFloat, "topk_weights must be fp32");
     a.topk_w = topk_w->data_ptr<float>();
   }
+  if (nte.has_value()) {
+    TORCH_CHECK(nte->is_contiguous() && nte->scalar_type() == at::kInt && nte->numel() == num_experts,
+                "num_tokens_per_expert must be a contiguous [E] int32 tensor");
+    a.nte = nte->data_ptr<int32_t>();
+    a.has_nte = 1;
+  }
   a.in_rank = in_rank.data_ptr<bool>();
   a.token_pos = token_pos.data_ptr<int32_t>();
   a.recv_off = recv_off.data_ptr<int64_t>();
   a.E = static_cast<int>(num_experts);
   a.ticket = static_cast<uint64_t>(ticket);
+  a.local_direct = mode != 2 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (a.x_stride & 15) == 0 &&
+                   (mode == 0 || ((reinterpret_cast<uintptr_t>(a.xs) & 15) == 0 && (a.xs_stride * 4) % 16 == 0));
   int grid = num_sms > 0 ? static_cast<int>(num_sms) : heap.num_sms();
   grid = std::max(1, std::min(grid, std::max(1, a.T / 2 + 1)));
   nd_prepare_kernel<<<grid, kPrepThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
@@ -310,6 +320,10 @@ struct NdPullArgs {
   int mode, H, K, E;
   int use_tma, nstages;
   int stage_bytes;
+  const uint8_t* local_x;      // rows from this rank come straight from x (null: use staging)
+  int64_t local_x_stride;      // bytes
+  const uint8_t* local_scales; // fp8 tuple input: scales rows
+  int64_t local_scales_stride; // bytes
 };
 
 __global__ void __launch_bounds__(kPullThreads) nd_pull_kernel(NdPullArgs a) {
@@ -364,7 +378,8 @@ __global__ void __launch_bounds__(kPullThreads) nd_pull_kernel(NdPullArgs a) {
 
     if (a.use_tma) {
       if (tid == 0 && tma_ok) {
-        auto src_of = [&](int q) {
+        auto src_of = [&](int q) -> const uint8_t* {
+          if (a.local_x && s_src[q] == me) return a.local_x + static_cast<int64_t>(s_tok[q]) * a.local_x_stride;
           return hv.base[s_src[q]] + hv.L.nd_x[slot] + static_cast<int64_t>(s_tok[q]) * rs;
         };
         auto issue = [&](int q) {
@@ -395,7 +410,9 @@ __global__ void __launch_bounds__(kPullThreads) nd_pull_kernel(NdPullArgs a) {
       }
     } else {
       for (int q = warp; q < n; q += nwarps) {
-        const uint8_t* src = hv.base[s_src[q]] + hv.L.nd_x[slot] + static_cast<int64_t>(s_tok[q]) * rs;
+        const uint8_t* src = (a.local_x && s_src[q] == me)
+                                 ? a.local_x + static_cast<int64_t>(s_tok[q]) * a.local_x_stride
+                                 : hv.base[s_src[q]] + hv.L.nd_x[slot] + static_cast<int64_t>(s_tok[q]) * rs;
         warp_copy(a.recv_x + (chunk + q) * MD, src, MD);
       }
     }
@@ -422,7 +439,9 @@ __global__ void __launch_bounds__(kPullThreads) nd_pull_kernel(NdPullArgs a) {
         if (a.recv_w) a.recv_w[o] = local ? ld_volatile_f32(hv.at<float>(s, hv.L.nd_w[slot]) + ki) : 0.f;
       }
       if (SB) {
-        const uint8_t* src = hv.base[s] + hv.L.nd_x[slot] + static_cast<int64_t>(t) * rs + H;
+        const uint8_t* src = (a.local_x && s == me)
+                                 ? a.local_scales + static_cast<int64_t>(t) * a.local_scales_stride
+                                 : hv.base[s] + hv.L.nd_x[slot] + static_cast<int64_t>(t) * rs + H;
         warp_copy(reinterpret_cast<uint8_t*>(a.recv_scales) + i * SB, src, SB);
       }
     }
@@ -433,7 +452,7 @@ __global__ void __launch_bounds__(kPullThreads) nd_pull_kernel(NdPullArgs a) {
 
 void nd_pull(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_scales, const OptTensor& recv_topk,
              const OptTensor& recv_w, at::Tensor recv_src, int64_t mode, int64_t num_experts, int64_t num_sms,
-             bool use_tma) {
+             bool use_tma, const OptTensor& local_x, const OptTensor& local_scales) {
   const c10::cuda::CUDAGuard guard(recv_x.device());
   HeapView hv = heap.view();
   NdPullArgs a{};
@@ -457,6 +476,23 @@ void nd_pull(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_scales, co
   if (recv_w.has_value()) a.recv_w = recv_w->data_ptr<float>();
   a.recv_src = recv_src.data_ptr();
   a.recv_src_i32 = recv_src.scalar_type() == at::kInt;
+  // same rule as nd_prepare's local_direct: rows for this rank were not staged in that case
+  if (local_x.has_value() && mode != 2) {
+    const uintptr_t xp = reinterpret_cast<uintptr_t>(local_x->data_ptr());
+    const int64_t xs = local_x->stride(0) * local_x->element_size();
+    bool ok = (xp & 15) == 0 && (xs & 15) == 0;
+    if (mode == 1) {
+      TORCH_CHECK(local_scales.has_value(), "fp8 input needs its scales");
+      const uintptr_t sp = reinterpret_cast<uintptr_t>(local_scales->data_ptr());
+      ok = ok && (sp & 15) == 0 && (local_scales->stride(0) * 4) % 16 == 0;
+      a.local_scales = static_cast<const uint8_t*>(local_scales->data_ptr());
+      a.local_scales_stride = local_scales->stride(0) * 4;
+    }
+    if (ok) {
+      a.local_x = static_cast<const uint8_t*>(local_x->data_ptr());
+      a.local_x_stride = xs;
+    }
+  }
   const int64_t MD = mode == 0 ? 2LL * a.H : a.H;
   const bool aligned = (reinterpret_cast<uintptr_t>(a.recv_x) & 15) == 0 && (MD % 16) == 0 && MD < (1 << 20);
   a.use_tma = use_tma && aligned;
@@ -525,7 +561,7 @@ __global__ void __launch_bounds__(kCombThreads) nc_combine_kernel(NcArgs a) {
     int s = 0;
     while (s + 1 < R && s_off[s + 1] <= i) ++s;
     const int64_t j = i - s_off[s];
-    if (j >= M) continue;
+    if (j >= M || s == me) continue;  // own rows are read from x in place by the reduce
     const int64_t slot_row = static_cast<int64_t>(me) * M + j;
     warp_copy(hv.at<uint8_t>(s, hv.L.nc_rows[slot]) + slot_row * RB, a.x + i * a.x_stride, RB);
     if (a.w && lane < K) hv.at<float>(s, hv.L.nc_w[slot])[slot_row * K + lane] = a.w[i * a.w_stride + lane];
@@ -539,8 +575,10 @@ __global__ void __launch_bounds__(kCombThreads) nc_combine_kernel(NcArgs a) {
   }
   __syncthreads();
   if (s_last) {
-    fence_sys();
-    if (tid < R) st_release_sys(&hv.sig(tid)->nc_ready[slot][me], e);
+    if (tid < R) {
+      fence_sys();
+      st_release_sys(&hv.sig(tid)->nc_ready[slot][me], e);
+    }
     if (tid == 0) {
       ls->arrive[kEpNC] = 0;
       ls->epoch[kEpNC] = e;
@@ -552,9 +590,8 @@ __global__ void __launch_bounds__(kCombThreads) nc_combine_kernel(NcArgs a) {
     if (!wait_epoch(&hv.sig(me)->nc_ready[slot][tid], e, hv.timeout_ns, hv.status, kTimeoutCombine, 3, me, tid))
       atomicExch(&s_fail, 1);
   }
-  __syncthreads();
+  __syncthreads();  // every thread reads rows whose flags threads < R acquired
   if (s_fail) return;
-  fence_sys();
   const uint8_t* rows = hv.at<uint8_t>(me, hv.L.nc_rows[slot]);
   const float* wrows = hv.at<float>(me, hv.L.nc_w[slot]);
   const bool vec = (H % 8) == 0;
@@ -568,21 +605,42 @@ __global__ void __launch_bounds__(kCombThreads) nc_combine_kernel(NcArgs a) {
     const T16* b0 = a.bias0 ? reinterpret_cast<const T16*>(a.bias0) + static_cast<int64_t>(t) * H : nullptr;
     const T16* b1 = a.bias1 ? reinterpret_cast<const T16*>(a.bias1) + static_cast<int64_t>(t) * H : nullptr;
     if (vec) {
-      for (int c = lane * 8; c < H; c += 256) {
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int r = 0; r < R; ++r) {
-          const int p = pos[r];
-          if (p < 0) continue;
-          const int4 v = *reinterpret_cast<const int4*>(rows + (static_cast<int64_t>(r) * M + p) * RB + c * 2);
-          acc8<T16>(acc, v);
-        }
-        if (b0) acc8<T16>(acc, *reinterpret_cast<const int4*>(b0 + c));
-        if (b1) acc8<T16>(acc, *reinterpret_cast<const int4*>(b1 + c));
-        int4 o;
-        T16* oh = reinterpret_cast<T16*>(&o);
+      // rows of this token present in the return blocks
+      const uint8_t* rp[B200EP_MAX_RANKS];
+      int nr = 0;
+      for (int r = 0; r < R; ++r) {
+        if (pos[r] < 0) continue;
+        rp[nr++] = r == me ? a.x + (s_off[me] + pos[r]) * a.x_stride
+                           : rows + (static_cast<int64_t>(r) * M + pos[r]) * RB;
+      }
+      // four 256-element chunks per pass: up to 4 x nr independent 16-byte loads per lane
+      for (int c0 = lane * 8; c0 < H; c0 += 1024) {
+        float acc[4][8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) oh[i] = static_cast<T16>(acc[i]);
-        *reinterpret_cast<int4*>(out + c) = o;
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[u][i] = 0.f;
+        for (int r = 0; r < nr; ++r) {
+          int4 v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (c0 + u * 256 < H) v[u] = *reinterpret_cast<const int4*>(rp[r] + (c0 + u * 256) * 2);
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (c0 + u * 256 < H) acc8<T16>(acc[u], v[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = c0 + u * 256;
+          if (c >= H) continue;
+          if (b0) acc8<T16>(acc[u], *reinterpret_cast<const int4*>(b0 + c));
+          if (b1) acc8<T16>(acc[u], *reinterpret_cast<const int4*>(b1 + c));
+          int4 o;
+          T16* oh = reinterpret_cast<T16*>(&o);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) oh[i] = static_cast<T16>(acc[u][i]);
+          *reinterpret_cast<int4*>(out + c) = o;
+        }
       }
     } else {
       for (int c = lane; c < H; c += 32) {
@@ -590,8 +648,9 @@ __global__ void __launch_bounds__(kCombThreads) nc_combine_kernel(NcArgs a) {
         for (int r = 0; r < R; ++r) {
           const int p = pos[r];
           if (p < 0) continue;
-          acc += static_cast<float>(
-              reinterpret_cast<const T16*>(rows + (static_cast<int64_t>(r) * M + p) * RB)[c]);
+          const uint8_t* row = r == me ? a.x + (s_off[me] + p) * a.x_stride
+                                       : rows + (static_cast<int64_t>(r) * M + p) * RB;
+          acc += static_cast<float>(reinterpret_cast<const T16*>(row)[c]);
         }
         if (b0) acc += static_cast<float>(b0[c]);
         if (b1) acc += static_cast<float>(b1[c]);
@@ -602,7 +661,8 @@ __global__ void __launch_bounds__(kCombThreads) nc_combine_kernel(NcArgs a) {
       float s = 0.f;
       for (int r = 0; r < R; ++r) {
         const int p = pos[r];
-        if (p >= 0) s += wrows[(static_cast<int64_t>(r) * M + p) * K + lane];
+        if (p < 0) continue;
+        s += r == me ? a.w[(s_off[me] + p) * a.w_stride + lane] : wrows[(static_cast<int64_t>(r) * M + p) * K + lane];
       }
       a.out_w[static_cast<int64_t>(t) * K + lane] = s;
     }

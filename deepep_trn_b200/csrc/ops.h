@@ -57,11 +57,11 @@ void layout(const at::Tensor& topk_idx, int64_t num_experts, int64_t num_ranks, 
 
 // normal.cu
 void nd_prepare(SymmHeap& heap, const at::Tensor& x, const OptTensor& x_scales, int64_t mode, bool round_scale,
-                const OptTensor& topk_idx, const OptTensor& topk_w, const at::Tensor& in_rank, at::Tensor token_pos,
-                at::Tensor recv_off, int64_t num_experts, int64_t ticket, int64_t num_sms);
+                const OptTensor& topk_idx, const OptTensor& topk_w, const OptTensor& nte, const at::Tensor& in_rank,
+                at::Tensor token_pos, at::Tensor recv_off, int64_t num_experts, int64_t ticket, int64_t num_sms);
 void nd_pull(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_scales, const OptTensor& recv_topk,
              const OptTensor& recv_w, at::Tensor recv_src, int64_t mode, int64_t num_experts, int64_t num_sms,
-             bool use_tma);
+             bool use_tma, const OptTensor& local_x, const OptTensor& local_scales);
 void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const at::Tensor& recv_off,
                 const at::Tensor& token_pos, at::Tensor out, const OptTensor& out_w, const OptTensor& bias0,
                 const OptTensor& bias1, int64_t num_sms);
@@ -80,6 +80,24 @@ void ll_combine_recv(SymmHeap& heap, const at::Tensor& topk_idx, const at::Tenso
 // diag.cu
 void device_barrier(SymmHeap& heap);
 void wait_probe(SymmHeap& heap, int64_t budget_ns);
+
+// gemm.cu
+void grouped_gemm_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, const OptTensor& C,
+                    const OptTensor& Hout, int64_t epilogue, at::Tensor error, int64_t num_sms, double timeout_s);
+void grouped_gemm_k(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, at::Tensor C,
+                    at::Tensor error, int64_t num_sms, double timeout_s);
+
+// moe.cu
+void router_topk(const at::Tensor& logits, int64_t topk, at::Tensor idx, at::Tensor w);
+void router_topk_bwd(const at::Tensor& idx, const at::Tensor& w, const at::Tensor& dw, at::Tensor dlogits);
+void permute(const at::Tensor& x, const at::Tensor& ids, int64_t num_local_experts, at::Tensor out, at::Tensor pos,
+             at::Tensor offsets, at::Tensor counts, at::Tensor scratch);
+void unpermute(const at::Tensor& rows, const at::Tensor& pos, const at::Tensor& w, at::Tensor y);
+void unpermute_bwd(const at::Tensor& dy, const at::Tensor& rows, const at::Tensor& pos, const at::Tensor& w,
+                   at::Tensor drows, const OptTensor& dw, const at::Tensor& offsets, const at::Tensor& counts);
+void permute_bwd(const at::Tensor& drows, const at::Tensor& pos, at::Tensor dx);
+void swiglu_bwd(const at::Tensor& dh, const at::Tensor& pre, at::Tensor dpre);
+void transpose(const at::Tensor& in, at::Tensor out);
 
 // quant.cu
 void quant_fp8(const at::Tensor& x, at::Tensor q, at::Tensor scales, bool round_scale);

@@ -1,0 +1,130 @@
+"""Expert-parallel MoE layer: router top-k -> dispatch -> grouped SwiGLU experts -> combine.
+
+Forward (per rank, EP group of the Buffer):
+    logits = x @ Wr^T ; (idx, w) = router_topk(logits)               # N9
+    recv = dispatch(x)  (normal mode, NVLink kernels)                 # N1 + N2
+    rows = permute(recv) into 128-row padded expert segments          # N10
+    h, pre = grouped_gemm(rows, W1, swiglu epilogue)                  # N7 + N8 (tcgen05)
+    o = grouped_gemm(h, W2)                                           # N7
+    y_recv = unpermute(o, weights)                                    # N10
+    y = combine(y_recv)                                               # N3
+Backward reuses the dispatch handle: the gradient of combine is a cached dispatch
+and the gradient of dispatch is a combine (whose weight channel carries the
+routing-weight gradients home). Expert weight gradients come from the variable-K
+grouped GEMM over the permuted activations.
+
+Weights: W1 [EL, 2I, H] with gate and up rows interleaved in 128-row blocks
+(``ops.gemm.interleave_gate_up``), W2 [EL, H, I], router Wr [E, H]; all bf16.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from ..ops import gemm as G
+from ..ops import moe_ops as MO
+
+
+def _expert_forward(rows, offsets, W1, W2):
+    h, pre = G.grouped_gemm(rows, W1, offsets, epilogue='swiglu')
+    o = G.grouped_gemm(h, W2, offsets)
+    return h, pre, o
+
+
+class _MoEFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, Wr, W1, W2, buf, num_experts, topk):
+        EL = num_experts // buf.group_size
+        logits = (x @ Wr.t()).float()
+        idx, w = MO.router_topk(logits, topk)
+        ntr, _, nte, itr, _ = buf.get_dispatch_layout(idx, num_experts)
+        recv_x, recv_idx, recv_w, per_expert, handle, _ = buf.dispatch(
+            x, topk_idx=idx, topk_weights=w, num_tokens_per_rank=ntr, is_token_in_rank=itr,
+            num_tokens_per_expert=nte)
+        rows, pos, offsets, counts = MO.permute(recv_x, recv_idx, EL, per_expert)
+        h, pre, o = _expert_forward(rows, offsets, W1, W2)
+        y_recv = MO.unpermute(o, pos, recv_w)
+        y, _, _ = buf.combine(y_recv, handle)
+        ctx.save_for_backward(x, Wr, W1, W2, idx, w, recv_w, pos, offsets, counts, rows, pre, h, o)
+        ctx.buf, ctx.handle, ctx.num_experts = buf, handle, num_experts
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, Wr, W1, W2, idx, w, recv_w, pos, offsets, counts, rows, pre, h, o = ctx.saved_tensors
+        buf, handle = ctx.buf, ctx.handle
+        dy = dy.contiguous().to(x.dtype)
+        dy_recv, *_ = buf.dispatch(dy, handle=handle)                 # combine backward
+        d_o, d_recv_w = MO.unpermute_bwd(dy_recv, o, pos, recv_w, offsets, counts)
+        dh = G.grouped_gemm(d_o, MO.transpose(W2), offsets)            # [P, I]
+        dpre = MO.swiglu_bwd(dh, pre)                                  # [P, 2I]
+        drows = G.grouped_gemm(dpre, MO.transpose(W1), offsets)        # [P, H]
+        dW2 = G.grouped_gemm_wgrad(MO.transpose(d_o), MO.transpose(h), offsets, out_dtype=torch.float32)
+        dW1 = G.grouped_gemm_wgrad(MO.transpose(dpre), MO.transpose(rows), offsets, out_dtype=torch.float32)
+        d_recv_x = MO.permute_bwd(drows, pos)
+        dx, dw, _ = buf.combine(d_recv_x, handle, topk_weights=d_recv_w)   # dispatch backward
+        dlogits = MO.router_topk_bwd(idx, w, dw.float(), ctx.num_experts)
+        dx = (dx.float() + dlogits @ Wr.float()).to(x.dtype)
+        dWr = (dlogits.t() @ x.float()).to(Wr.dtype)
+        return dx, dWr, dW1.to(W1.dtype), dW2.to(W2.dtype), None, None, None
+
+
+class MoELayer(nn.Module):
+    """SwiGLU mixture-of-experts layer with expert parallelism over ``buffer``'s EP group."""
+
+    def __init__(self, buffer, hidden: int, intermediate: int, num_experts: int, topk: int,
+                 dtype=torch.bfloat16, device=None, init_std: float = 0.02, seed: int = 0):
+        super().__init__()
+        R = buffer.group_size
+        if num_experts % R:
+            raise ValueError(f'num_experts={num_experts} must be divisible by the EP size {R}')
+        if intermediate % 128 or hidden % 128:
+            raise ValueError('hidden and intermediate must be multiples of 128')
+        self.buffer = buffer
+        self.hidden, self.intermediate = hidden, intermediate
+        self.num_experts, self.topk = num_experts, topk
+        EL = num_experts // R
+        g = torch.Generator().manual_seed(seed)
+        g_local = torch.Generator().manual_seed(seed * 1000 + buffer.rank + 1)
+        std = init_std
+        self.router = nn.Parameter((torch.randn(num_experts, hidden, generator=g) * std).to(dtype).to(device))
+        wg = torch.randn(EL, intermediate, hidden, generator=g_local) * std
+        wu = torch.randn(EL, intermediate, hidden, generator=g_local) * std
+        self.w1 = nn.Parameter(G.interleave_gate_up(wg, wu).to(dtype).to(device))
+        self.w2 = nn.Parameter((torch.randn(EL, hidden, intermediate, generator=g_local) * std).to(dtype).to(device))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return _MoEFunction.apply(x, self.router, self.w1, self.w2, self.buffer, self.num_experts, self.topk)
+
+
+def reference_moe(x, Wr, W1, W2, topk):
+    """fp32 torch definition of the layer on one rank holding all experts (W1 interleaved)."""
+    logits = x.float() @ Wr.float().t()
+    idx, w = MO.router_topk(logits.cpu(), topk)
+    idx, w = idx.to(x.device), w.to(x.device)
+    out = torch.zeros(x.shape, dtype=torch.float32, device=x.device)
+    for e in range(W1.shape[0]):
+        hit = (idx == e)
+        tok = hit.any(1).nonzero().flatten()
+        if tok.numel() == 0:
+            continue
+        a = x[tok].float()
+        gu = a @ W1[e].float().t()
+        gate, up = G.deinterleave(gu)
+        hh = torch.nn.functional.silu(gate) * up
+        oo = hh @ W2[e].float().t()
+        we = (w[tok] * hit[tok]).sum(1, keepdim=True)
+        out[tok] += we * oo
+    return out
+
+
+def smoke_step(buf, dev):
+    """One tiny forward + backward of the layer (used by the build/smoke entry point)."""
+    torch.manual_seed(0)
+    layer = MoELayer(buf, hidden=256, intermediate=256, num_experts=8 * buf.group_size, topk=2, device=dev)
+    x = (torch.randn(64, 256, device=dev) * 0.5).to(torch.bfloat16).requires_grad_()
+    y = layer(x)
+    y.float().square().mean().backward()
+    torch.cuda.synchronize()
+    assert torch.isfinite(y.float()).all() and torch.isfinite(x.grad.float()).all()
+    assert layer.w1.grad is not None and torch.isfinite(layer.w1.grad.float()).all()

@@ -1,0 +1,75 @@
+"""Grouped expert GEMMs on tcgen05 tensor cores (N7) with fused SwiGLU (N8).
+
+``grouped_gemm``       C[seg_e] = A[seg_e] @ B[e]^T      A [rows, K], B [G, N, K]   (forward, dX)
+``grouped_gemm_wgrad`` C[e] = A[:, seg_e] @ B[:, seg_e]^T A [M, tok], B [N, tok]    (dW)
+
+Segments are given by ``offsets`` [G + 1] int64 on the device, multiples of 128
+(``permute`` pads every expert's rows to that). The kernels read the offsets on
+the device, so the calls are CUDA-graph capturable. A device error word records
+a timed-out wait inside a kernel; ``check()`` raises on it.
+"""
+from __future__ import annotations
+
+import torch
+
+from ._ext import load
+
+_errors: dict = {}
+EPILOGUES = {'bf16': 0, 'f32': 1, 'swiglu': 2}
+
+
+def _err(dev) -> torch.Tensor:
+    key = (dev.type, dev.index)
+    if key not in _errors:
+        _errors[key] = torch.zeros(1, dtype=torch.int32, device=dev)
+    return _errors[key]
+
+
+def check(device=None) -> None:
+    dev = device or torch.device('cuda', torch.cuda.current_device())
+    e = _err(dev)
+    if int(e.item()):
+        e.zero_()
+        raise RuntimeError('grouped GEMM: a pipeline wait timed out on the device')
+
+
+def grouped_gemm(A: torch.Tensor, B: torch.Tensor, offsets: torch.Tensor, out: torch.Tensor | None = None,
+                 epilogue: str = 'bf16', h_out: torch.Tensor | None = None, save_preact: bool = True,
+                 num_sms: int = 0, timeout_s: float = 10.0):
+    """Returns C (or ``(h, pre_activation)`` for ``epilogue='swiglu'``)."""
+    rows, N = A.shape[0], B.shape[1]
+    if epilogue == 'swiglu':
+        h = h_out if h_out is not None else torch.empty(rows, N // 2, dtype=torch.bfloat16, device=A.device)
+        c = (out if out is not None else torch.empty(rows, N, dtype=torch.bfloat16, device=A.device)) \
+            if save_preact else None
+        load().grouped_gemm_m(A, B, offsets, c, h, 2, _err(A.device), num_sms, timeout_s)
+        return h, c
+    dtype = torch.float32 if epilogue == 'f32' else torch.bfloat16
+    c = out if out is not None else torch.empty(rows, N, dtype=dtype, device=A.device)
+    load().grouped_gemm_m(A, B, offsets, c, None, EPILOGUES[epilogue], _err(A.device), num_sms, timeout_s)
+    return c
+
+
+def grouped_gemm_wgrad(A: torch.Tensor, B: torch.Tensor, offsets: torch.Tensor, out_dtype=torch.float32,
+                       out: torch.Tensor | None = None, num_sms: int = 0, timeout_s: float = 10.0):
+    G = offsets.numel() - 1
+    c = out if out is not None else torch.empty(G, A.shape[0], B.shape[0], dtype=out_dtype, device=A.device)
+    load().grouped_gemm_k(A, B, offsets, c, _err(A.device), num_sms, timeout_s)
+    return c
+
+
+def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor, block: int = 128) -> torch.Tensor:
+    """[G, I, K] gate and up weights -> [G, 2I, K] with 128-row blocks alternating gate / up,
+    the layout the SwiGLU epilogue expects (each 256-wide output tile = 128 gate + 128 up)."""
+    G, I, K = w_gate.shape
+    assert I % block == 0
+    g = w_gate.reshape(G, I // block, block, K)
+    u = w_up.reshape(G, I // block, block, K)
+    return torch.stack([g, u], 2).reshape(G, 2 * I, K)
+
+
+def deinterleave(x: torch.Tensor, block: int = 128):
+    """Inverse of the interleaving along the last dim: [.., 2I] -> (gate [.., I], up [.., I])."""
+    *lead, n2 = x.shape
+    v = x.reshape(*lead, n2 // (2 * block), 2, block)
+    return v[..., 0, :].reshape(*lead, n2 // 2), v[..., 1, :].reshape(*lead, n2 // 2)

@@ -126,7 +126,7 @@ class NvlinkEngine:
 
     # ------------------------------------------------------------------ normal mode
     def dispatch(self, x, handle, topk_idx, topk_weights, is_token_in_rank, num_experts, expert_alignment,
-                 num_worst_tokens, config, use_fp8=False, round_scale=False):
+                 num_worst_tokens, config, use_fp8=False, round_scale=False, num_tokens_per_expert=None):
         self.check()
         fp8_in = isinstance(x, tuple)
         xt = x[0] if fp8_in else x
@@ -138,7 +138,13 @@ class NvlinkEngine:
         else:
             K = topk_idx.shape[1]
             E = num_experts
-            itr = is_token_in_rank if is_token_in_rank is not None else self.get_dispatch_layout(topk_idx, E)[2]
+            nte = num_tokens_per_expert
+            if is_token_in_rank is None or nte is None:
+                _, lnte, litr = self.get_dispatch_layout(topk_idx, E)
+                itr = is_token_in_rank if is_token_in_rank is not None else litr
+                nte = nte if nte is not None else lnte
+            else:
+                itr = is_token_in_rank
         EL = experts_per_rank(E, self.R)
         self._ensure(self._spec(H, K, E))
         mode = 1 if fp8_in else (2 if use_fp8 else 0)
@@ -146,11 +152,13 @@ class NvlinkEngine:
         recv_off = torch.empty(self.R + 1, dtype=torch.int64, device=dev)
         self.ticket += 1
         nsm = self._sms(config)
+        x_scales = x[1].float().contiguous() if fp8_in else None
         with timer.stage('prepare'):
             self.C.nd_prepare(self.heap, xt if not fp8_in else xt.view(torch.uint8),
-                              x[1].float().contiguous() if fp8_in else None, mode, bool(round_scale),
+                              x_scales, mode, bool(round_scale),
                               None if cached else topk_idx.contiguous(),
                               None if (cached or topk_weights is None) else topk_weights.float().contiguous(),
+                              None if cached else nte.to(torch.int32).contiguous(),
                               itr.contiguous(), token_pos, recv_off, E, self.ticket, nsm)
         # Outputs are sized for the worst case (every peer sends its full capacity) so the pull
         # kernel can be queued before the host learns the receive size; the host then waits
@@ -177,7 +185,9 @@ class NvlinkEngine:
         if os.environ.get('B200EP_NO_TMA'):
             use_tma = False
         with timer.stage('pull'):
-            self.C.nd_pull(self.heap, recv_x, recv_s, recv_topk, recv_w, recv_src, mode, E, nsm, use_tma)
+            self.C.nd_pull(self.heap, recv_x, recv_s, recv_topk, recv_w, recv_src, mode, E, nsm, use_tma,
+                           xt if mode == 0 else (xt.view(torch.uint8) if mode == 1 else None),
+                           x_scales)
         per_expert = recv_counts = None
         if num_worst_tokens or cached:
             N = cap

@@ -100,12 +100,15 @@ def quantize_fp8_1x128(x: torch.Tensor, round_scale: bool = False):
         raise ValueError(f'hidden={H} must be a multiple of {FP8_BLOCK} for fp8 block scales')
     xf = x.float().reshape(*x.shape[:-1], H // FP8_BLOCK, FP8_BLOCK)
     amax = xf.abs().amax(-1).clamp_min(FP8_AMAX_FLOOR)
+    # IEEE divisions tensor by tensor (a python scalar on the left would become
+    # reciprocal-then-multiply in torch and round differently from the kernel)
+    c448 = torch.full_like(amax, FP8_MAX)
     if round_scale:
-        scale = _pow2_ceil(amax / FP8_MAX)
-        inv = 1.0 / scale
+        scale = _pow2_ceil(torch.div(amax, c448))
+        inv = torch.div(torch.ones_like(scale), scale)
     else:
-        scale = amax / FP8_MAX
-        inv = FP8_MAX / amax
+        scale = torch.div(amax, c448)
+        inv = torch.div(c448, amax)
     q = (xf * inv.unsqueeze(-1)).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
     return q.reshape(x.shape), scale
 
