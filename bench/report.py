@@ -1,0 +1,76 @@
+"""Aggregate a results directory into summary.md and ops.csv (reference: bench/report.py).
+
+python bench/report.py results/<run_id>
+"""
+from __future__ import annotations
+
+import csv
+import json
+import sys
+from pathlib import Path
+
+
+def load(run: Path, prefix: str) -> list[dict]:
+    rows = []
+    for path in sorted(run.glob(f'{prefix}_ep*.jsonl')):
+        rows += [json.loads(line) for line in path.read_text().splitlines() if line.strip()]
+    return rows
+
+
+def med(d):
+    return d['median_us'] if d else None
+
+
+def fmt(v):
+    if v is None:
+        return '-'
+    return f'{v:.2f}' if isinstance(v, float) else str(v)
+
+
+def table(header, rows):
+    out = ['| ' + ' | '.join(header) + ' |', '|' + '---|' * len(header)]
+    out += ['| ' + ' | '.join(fmt(c) for c in r) + ' |' for r in rows]
+    return '\n'.join(out)
+
+
+def main():
+    run = Path(sys.argv[1])
+    ops, tr, bl = load(run, 'ops'), load(run, 'transport'), load(run, 'baselines')
+    env = json.loads((run / 'env.json').read_text()) if (run / 'env.json').exists() else {}
+    parts = [f'# deepep_trn_b200 benchmark: {run.name}', '', f'- env: {env}', '',
+             'Device time (CUDA events), max over ranks, median of rounds. Logical bytes follow deep_ep '
+             '(normal: received rows x H x 2; LL: selected experts x H x 2).', '']
+    if ops:
+        rows = [[r['mode'], r['preset'], r['ep'], r['tokens'], r['routing'], r.get('fp8'),
+                 'PASS' if r['check']['passed'] else 'FAIL', med(r['device_us']['dispatch']),
+                 med(r['device_us']['combine']), med(r['device_us']['dispatch_combine']),
+                 med(r['latency_us']['dispatch']), med(r['latency_us']['combine']),
+                 r['gbps_per_rank']['dispatch_combine'], r['recv_load']['imbalance']]
+                for r in sorted(ops, key=lambda r: (r['mode'], r['preset'], r['ep'], r['tokens'], r['routing']))]
+        parts += ['## Ops', '', table(['mode', 'preset', 'EP', 'T/rank', 'routing', 'fp8', 'check', 'dispatch us',
+                                       'combine us', 'd+c us', 'latency d us', 'latency c us', 'GB/s/rank d+c',
+                                       'imbalance'], rows), '']
+        with open(run / 'ops.csv', 'w', newline='') as f:
+            w = csv.writer(f)
+            w.writerow(['mode', 'preset', 'ep', 'tokens', 'routing', 'fp8', 'check', 'dispatch_us', 'combine_us',
+                        'dc_us', 'gbps_rank_dc'])
+            for r in ops:
+                w.writerow([r['mode'], r['preset'], r['ep'], r['tokens'], r['routing'], r.get('fp8'),
+                            r['check']['passed'], med(r['device_us']['dispatch']), med(r['device_us']['combine']),
+                            med(r['device_us']['dispatch_combine']), r['gbps_per_rank']['dispatch_combine']])
+    if tr:
+        rows = [[r['ep'], r['hidden'], r['rows_per_peer'], r['fill'], r['tma'], med(r['device_us']),
+                 r['payload_gbps'], r['off_rank_gbps']] for r in tr]
+        parts += ['## Transport (dispatch pull) curve', '',
+                  table(['EP', 'H', 'rows/peer', 'fill', 'tma', 'us', 'payload GB/s', 'off-rank GB/s'], rows), '']
+    if bl:
+        rows = [[r['op'], r['preset'], r['ep'], r['tokens'], med(r.get('device_us')), med(r.get('latency_us')),
+                 r.get('error', '')] for r in bl]
+        parts += ['## NCCL collective baselines', '',
+                  table(['op', 'preset', 'EP', 'T/rank', 'pipelined us', 'latency us', 'error'], rows), '']
+    (run / 'summary.md').write_text('\n'.join(parts))
+    print(f'wrote {run / "summary.md"}')
+
+
+if __name__ == '__main__':
+    main()

@@ -55,4 +55,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("transpose", &transpose);
   m.def("grouped_gemm_k", &grouped_gemm_k);
   m.def("wait_probe", &wait_probe);
+  m.def("fence_cost", &fence_cost);
 }

@@ -4,7 +4,7 @@
 //   (ld.acquire.sys / st.release.sys / red.release.sys),
 // * bounded waits on %globaltimer that record an error in a host-mapped status
 //   page and return instead of trapping or hanging,
-// * TMA bulk copies (cp.async.bulk, no tensor map, never .multicast::cluster)
+// * TMA bulk copies (cp.async.bulk, no tensor map; every CTA fetches its own data)
 //   completed through shared-memory mbarriers or bulk async-groups.
 #pragma once
 

@@ -9,7 +9,7 @@
 //
 // Per CTA (one per SM, persistent over tiles), 6 warps:
 //   warp 0      TMA producer: one elected thread streams A/B k-blocks (128B-swizzled
-//               boxes, no multicast) into a STAGES-deep shared-memory ring.
+//               boxes, each CTA loading its own) into a STAGES-deep shared-memory ring.
 //   warp 1      TMEM owner + MMA issuer: allocates 512 TMEM columns (two 128x256
 //               fp32 accumulators), one elected thread issues tcgen05.mma
 //               (M=128, N=BN, K=16) per 16-wide k slice and commits each stage
@@ -46,6 +46,7 @@ struct Args {
   void* H;                  // SwiGLU output [rows, N/2] bf16
   int64_t ldh;
   int64_t c_group_stride;   // GROUP_K: elements between experts' outputs
+  int64_t c_rows;           // GROUP_M: rows of C (and H); later tile rows are not stored
   uint32_t* error;          // device word, non-zero after a timeout
   uint64_t timeout_ns;
 };
@@ -148,7 +149,9 @@ template <bool GROUP_K, int BN>
 __device__ __forceinline__ bool tile_of(int t, const Args& a, const int64_t* offs, Tile& tl) {
   const int ntiles_n = (a.N + BN - 1) / BN;
   if (!GROUP_K) {
-    const int total_m = static_cast<int>((offs[a.G] < a.M ? offs[a.G] : a.M) / BM);
+    // tiles cover min(offsets[G], rows of A rounded up); rows past C are masked in the epilogue
+    const int64_t mpad = (static_cast<int64_t>(a.M) + BM - 1) / BM * BM;
+    const int total_m = static_cast<int>((offs[a.G] < mpad ? offs[a.G] : mpad) / BM);
     if (t >= total_m * ntiles_n) return false;
     const int mt = t / ntiles_n;
     tl.n0 = (t % ntiles_n) * BN;
@@ -290,6 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // tile = [128 gate columns | 128 up columns] of the interleaved weight layout
         __nv_bfloat16* hrow = static_cast<__nv_bfloat16*>(a.H) + grow * a.ldh + tl.n0 / 2;
         __nv_bfloat16* crow = a.C ? static_cast<__nv_bfloat16*>(a.C) + grow * a.ldc + tl.n0 : nullptr;
+        const bool srow = grow < a.c_rows;
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
           uint32_t g[32], u[32];
@@ -303,6 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             gv[i] = __float2bfloat16_rn(gf);
             uv[i] = __float2bfloat16_rn(uf);
           }
+          if (!srow) continue;
 #pragma unroll
           for (int i = 0; i < 4; ++i) reinterpret_cast<int4*>(hrow + c)[i] = reinterpret_cast<int4*>(hv)[i];
           if (crow) {
@@ -315,7 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
         const int64_t cbase = GROUP_K ? static_cast<int64_t>(tl.g) * a.c_group_stride : 0;
-        const bool rok = GROUP_K ? (tl.m0 + row < a.M) : true;
+        const bool rok = GROUP_K ? (tl.m0 + row < a.M) : (grow < a.c_rows);
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
@@ -433,13 +438,16 @@ void grouped_gemm_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
   a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
   const CUtensorMap ma = make_map(A.data_ptr(), A.size(0), a.K, A.stride(0), BM);
   const CUtensorMap mb = make_map(B.data_ptr(), int64_t(a.G) * a.N, a.K, a.K, 256);
+  a.c_rows = A.size(0);
   if (epilogue == kEpiSwiGLU) {
     TORCH_CHECK(a.N % 256 == 0 && Hout.has_value(), "SwiGLU needs N % 256 == 0 and an H output");
     a.H = Hout->data_ptr();
     a.ldh = Hout->stride(0);
+    TORCH_CHECK(Hout->size(0) >= A.size(0), "H needs as many rows as A");
   }
   if (C.has_value()) {
     TORCH_CHECK(C->size(0) >= A.size(0) && C->stride(1) == 1, "C needs at least as many rows as A");
+    TORCH_CHECK(epilogue != kEpiF32 || a.ldc % 4 == 0, "fp32 C rows must be 16-byte aligned");
     a.C = C->data_ptr();
     a.ldc = C->stride(0);
     TORCH_CHECK(a.ldc % 8 == 0 && (reinterpret_cast<uintptr_t>(a.C) & 15) == 0, "C rows must be 16-byte aligned");

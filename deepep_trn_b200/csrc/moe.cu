@@ -115,25 +115,28 @@ void router_topk_bwd(const at::Tensor& idx, const at::Tensor& w, const at::Tenso
 }
 
 // ============================================================================ permute
-constexpr int kPermRows = 256;     // rows per block of the count/scatter passes
+constexpr int kPermRows = 32;      // rows per block of the count/scatter passes (one warp)
 constexpr int kPermMaxExperts = 1024;
 
-// Per block: cnt[block][e] = #rows of the block routed to local expert e.
+// Per 32-row block: cnt[block][e] = #rows of the block routed to local expert e.
 template <typename IdxT>
-__global__ void __launch_bounds__(kPermRows) permute_count_kernel(const IdxT* __restrict__ ids, int N, int K, int EL,
-                                                                   int32_t* __restrict__ cnt) {
-  __shared__ int32_t s_cnt[kPermMaxExperts];
-  for (int e = threadIdx.x; e < EL; e += blockDim.x) s_cnt[e] = 0;
-  __syncthreads();
-  const int n = blockIdx.x * kPermRows + threadIdx.x;
-  if (n < N) {
-    for (int k = 0; k < K; ++k) {
+__global__ void __launch_bounds__(32) permute_count_kernel(const IdxT* __restrict__ ids, int N, int K, int EL,
+                                                            int32_t* __restrict__ cnt) {
+  const int lane = lane_id();
+  const int n = blockIdx.x * kPermRows + lane;
+  int32_t e_of[32];
+  for (int k = 0; k < 32; ++k) e_of[k] = -1;
+  if (n < N)
+    for (int k = 0; k < K && k < 32; ++k) {
       const int64_t e = static_cast<int64_t>(ids[static_cast<int64_t>(n) * K + k]);
-      if (e >= 0 && e < EL) atomicAdd(&s_cnt[e], 1);
+      e_of[k] = (e >= 0 && e < EL) ? static_cast<int32_t>(e) : -1;
     }
+  for (int e = 0; e < EL; ++e) {
+    bool has = false;
+    for (int k = 0; k < K && k < 32; ++k) has |= e_of[k] == e;
+    const uint32_t b = __ballot_sync(0xffffffffu, has);
+    if (lane == 0) cnt[static_cast<int64_t>(blockIdx.x) * EL + e] = __popc(b);
   }
-  __syncthreads();
-  for (int e = threadIdx.x; e < EL; e += blockDim.x) cnt[static_cast<int64_t>(blockIdx.x) * EL + e] = s_cnt[e];
 }
 
 // One CTA: padded segment offsets [EL + 1] and base[block][e] (first row of the block's rows of e).
@@ -168,45 +171,31 @@ __global__ void permute_scan_kernel(int32_t* __restrict__ cnt_base, int nblocks,
   }
 }
 
-// Per block: within-block order of (row, k) for each expert is row order (top-k ids are
-// distinct per row); row r of the block gets base + #earlier rows of the block with e.
+// Per 32-row block (one warp): the rows of expert e keep row order. Top-k ids are
+// distinct per row, so "row n has e" is one bit per lane and the lane prefix of the
+// ballot is the position within the block.
 template <typename IdxT>
-__global__ void __launch_bounds__(kPermRows) permute_scatter_kernel(
-    const IdxT* __restrict__ ids, int N, int K, int EL, const int32_t* __restrict__ base,
-    int32_t* __restrict__ pos) {
-  __shared__ int32_t s_run[kPermMaxExperts];
-  const int b = blockIdx.x;
-  for (int e = threadIdx.x; e < EL; e += blockDim.x) s_run[e] = base[static_cast<int64_t>(b) * EL + e];
-  __syncthreads();
-  // serialise rows of the block in order with one warp per 32-row slice and a
-  // ballot per expert hit: rows processed warp by warp keep row order
-  const int warp = warp_id(), lane = lane_id();
-  constexpr int nwarps = kPermRows / 32;
-  for (int w = 0; w < nwarps; ++w) {
-    if (warp == w) {
-      const int n = b * kPermRows + w * 32 + lane;
-      for (int k = 0; k < K; ++k) {
-        int64_t e = -1;
-        if (n < N) e = static_cast<int64_t>(ids[static_cast<int64_t>(n) * K + k]);
-        const bool ok = e >= 0 && e < EL;
-        // lanes sharing an expert in this round: order by lane (= row order)
-        const uint32_t same = __match_any_sync(0xffffffffu, ok ? static_cast<int>(e) : -1);
-        int p = -1;
-        if (ok) {
-          const int leader = __ffs(same) - 1;
-          const int rank_in = __popc(same & lanemask_lt());
-          int b0 = 0;
-          if (lane == leader) b0 = s_run[e];
-          b0 = __shfl_sync(same, b0, leader);
-          p = b0 + rank_in;
-          __syncwarp(same);
-          if (lane == leader) s_run[e] = b0 + __popc(same);
-        }
-        if (n < N) pos[static_cast<int64_t>(n) * K + k] = p;
-        __syncwarp();
-      }
+__global__ void __launch_bounds__(32) permute_scatter_kernel(const IdxT* __restrict__ ids, int N, int K, int EL,
+                                                              const int32_t* __restrict__ base,
+                                                              int32_t* __restrict__ pos) {
+  const int lane = lane_id();
+  const int n = blockIdx.x * kPermRows + lane;
+  int32_t e_of[32];
+  for (int k = 0; k < 32; ++k) e_of[k] = -1;
+  if (n < N)
+    for (int k = 0; k < K && k < 32; ++k) {
+      const int64_t e = static_cast<int64_t>(ids[static_cast<int64_t>(n) * K + k]);
+      e_of[k] = (e >= 0 && e < EL) ? static_cast<int32_t>(e) : -1;
+      pos[static_cast<int64_t>(n) * K + k] = -1;
     }
-    __syncthreads();
+  for (int e = 0; e < EL; ++e) {
+    int hit_k = -1;
+    for (int k = 0; k < K && k < 32; ++k)
+      if (e_of[k] == e) hit_k = k;
+    const uint32_t b = __ballot_sync(0xffffffffu, hit_k >= 0);
+    if (hit_k >= 0)
+      pos[static_cast<int64_t>(n) * K + hit_k] =
+          base[static_cast<int64_t>(blockIdx.x) * EL + e] + __popc(b & lanemask_lt());
   }
 }
 
@@ -243,20 +232,21 @@ void permute(const at::Tensor& x, const at::Tensor& ids, int64_t num_local_exper
   TORCH_CHECK(row_bytes % 16 == 0, "row bytes must be a multiple of 16");
   const int nblocks = std::max(1, (N + kPermRows - 1) / kPermRows);
   TORCH_CHECK(scratch.numel() >= int64_t(nblocks) * EL, "scratch too small");
+  TORCH_CHECK(K <= 32, "top-k above 32 is not supported by permute");
   auto s = at::cuda::getCurrentCUDAStream();
   int32_t* cb = scratch.data_ptr<int32_t>();
   if (ids.scalar_type() == at::kLong) {
-    permute_count_kernel<int64_t><<<nblocks, kPermRows, 0, s>>>(ids.data_ptr<int64_t>(), N, K, EL, cb);
+    permute_count_kernel<int64_t><<<nblocks, 32, 0, s>>>(ids.data_ptr<int64_t>(), N, K, EL, cb);
   } else {
-    permute_count_kernel<int32_t><<<nblocks, kPermRows, 0, s>>>(ids.data_ptr<int32_t>(), N, K, EL, cb);
+    permute_count_kernel<int32_t><<<nblocks, 32, 0, s>>>(ids.data_ptr<int32_t>(), N, K, EL, cb);
   }
   permute_scan_kernel<<<1, 1024, 0, s>>>(cb, nblocks, EL, 128, offsets.data_ptr<int64_t>(), counts.data_ptr<int32_t>());
   if (ids.scalar_type() == at::kLong) {
-    permute_scatter_kernel<int64_t><<<nblocks, kPermRows, 0, s>>>(ids.data_ptr<int64_t>(), N, K, EL, cb,
-                                                                  pos.data_ptr<int32_t>());
+    permute_scatter_kernel<int64_t><<<nblocks, 32, 0, s>>>(ids.data_ptr<int64_t>(), N, K, EL, cb,
+                                                           pos.data_ptr<int32_t>());
   } else {
-    permute_scatter_kernel<int32_t><<<nblocks, kPermRows, 0, s>>>(ids.data_ptr<int32_t>(), N, K, EL, cb,
-                                                                  pos.data_ptr<int32_t>());
+    permute_scatter_kernel<int32_t><<<nblocks, 32, 0, s>>>(ids.data_ptr<int32_t>(), N, K, EL, cb,
+                                                           pos.data_ptr<int32_t>());
   }
   const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
   permute_copy_kernel<<<sms * 4, 256, 0, s>>>(static_cast<const uint8_t*>(x.data_ptr()), x.stride(0) * x.element_size(),

@@ -84,52 +84,66 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
     if (blockIdx.x == 0 && tid == 0) report_error(hv.status, kCapacity, 1, me, -1, M, T);
   }
 
-  // ---------------------------------------------------------------- CTA 0: scan + expert counts
+  // ---------------------------------------------------------------- CTA 0: per-destination scan
+  // Each thread owns a contiguous chunk of tokens; one block-wide exclusive scan per
+  // destination gives every (token, destination) its row in that destination's list,
+  // in token order.
   if (blockIdx.x == 0) {
-    if (tid < B200EP_MAX_RANKS) s_base[tid] = 0;
-    __syncthreads();
-    for (int tile = 0; tile < T; tile += kPrepThreads) {
-      const int t = tile + tid;
-      uint32_t mask = 0;
-      if (t < T && t < M) {
-        const bool* row = a.in_rank + static_cast<int64_t>(t) * R;
-        for (int r = 0; r < R; ++r) mask |= (row[r] ? 1u : 0u) << r;
+    const int Tc = min(T, M);
+    const int tpt = (Tc + kPrepThreads - 1) / kPrepThreads;
+    const int c0 = min(Tc, tid * tpt), c1 = min(Tc, c0 + tpt);
+    int cnt[B200EP_MAX_RANKS];
+#pragma unroll
+    for (int r = 0; r < B200EP_MAX_RANKS; ++r) cnt[r] = 0;
+    for (int t = c0; t < c1; ++t) {
+      const bool* row = a.in_rank + static_cast<int64_t>(t) * R;
+#pragma unroll
+      for (int r = 0; r < B200EP_MAX_RANKS; ++r)
+        if (r < R && row[r]) ++cnt[r];
+    }
+    // warp inclusive scans, then warp offsets
+    int incl[B200EP_MAX_RANKS];
+#pragma unroll
+    for (int r = 0; r < B200EP_MAX_RANKS; ++r) {
+      if (r >= R) continue;
+      int v = cnt[r];
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += u;
       }
-      uint32_t bal[B200EP_MAX_RANKS];
+      incl[r] = v;
+      if (lane == 31) s_cnt[r][warp] = v;
+    }
+    __syncthreads();
+    if (tid < R) {
+      int run = 0;
+      for (int w = 0; w < nwarps; ++w) {
+        const int c = s_cnt[tid][w];
+        s_cnt[tid][w] = run;
+        run += c;
+      }
+      s_base[tid] = run;  // total rows for destination tid
+    }
+    __syncthreads();
+    int off[B200EP_MAX_RANKS];
+#pragma unroll
+    for (int r = 0; r < B200EP_MAX_RANKS; ++r)
+      if (r < R) off[r] = s_cnt[r][warp] + incl[r] - cnt[r];
+    for (int t = c0; t < c1; ++t) {
+      const bool* row = a.in_rank + static_cast<int64_t>(t) * R;
+      int32_t* pos_row = a.token_pos + static_cast<int64_t>(t) * R;
 #pragma unroll
       for (int r = 0; r < B200EP_MAX_RANKS; ++r) {
-        if (r < R) {
-          bal[r] = __ballot_sync(0xffffffffu, (mask >> r) & 1u);
-          if (lane == 0) s_cnt[r][warp] = __popc(bal[r]);
+        if (r >= R) continue;
+        if (row[r]) {
+          pos_row[r] = off[r];
+          stage_lists[static_cast<int64_t>(r) * M + off[r]] = t;
+          ++off[r];
+        } else {
+          pos_row[r] = -1;
         }
       }
-      __syncthreads();
-      if (tid < R) {
-        int run = s_base[tid];
-        for (int w = 0; w < nwarps; ++w) {
-          const int c = s_cnt[tid][w];
-          s_cnt[tid][w] = run;
-          run += c;
-        }
-        s_base[tid] = run;
-      }
-      __syncthreads();
-      if (t < T && t < M) {
-        int32_t* pos_row = a.token_pos + static_cast<int64_t>(t) * R;
-#pragma unroll
-        for (int r = 0; r < B200EP_MAX_RANKS; ++r) {
-          if (r < R) {
-            if ((mask >> r) & 1u) {
-              const int p = s_cnt[r][warp] + __popc(bal[r] & lanemask_lt());
-              pos_row[r] = p;
-              stage_lists[static_cast<int64_t>(r) * M + p] = t;
-            } else {
-              pos_row[r] = -1;
-            }
-          }
-        }
-      }
-      __syncthreads();
     }
     int32_t* stage_counts = hv.at<int32_t>(me, hv.L.nd_counts[slot]);
     int32_t* stage_nte = hv.at<int32_t>(me, hv.L.nd_nte[slot]);
@@ -613,24 +627,25 @@ __global__ void __launch_bounds__(kCombThreads) nc_combine_kernel(NcArgs a) {
         rp[nr++] = r == me ? a.x + (s_off[me] + pos[r]) * a.x_stride
                            : rows + (static_cast<int64_t>(r) * M + pos[r]) * RB;
       }
-      // four 256-element chunks per pass: up to 4 x nr independent 16-byte loads per lane
-      for (int c0 = lane * 8; c0 < H; c0 += 1024) {
-        float acc[4][8];
+      // eight 256-element chunks per pass: up to 8 x nr independent 16-byte loads per lane
+      constexpr int U = 8;
+      for (int c0 = lane * 8; c0 < H; c0 += 256 * U) {
+        float acc[U][8];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < U; ++u)
 #pragma unroll
           for (int i = 0; i < 8; ++i) acc[u][i] = 0.f;
         for (int r = 0; r < nr; ++r) {
-          int4 v[4];
+          int4 v[U];
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
+          for (int u = 0; u < U; ++u)
             if (c0 + u * 256 < H) v[u] = *reinterpret_cast<const int4*>(rp[r] + (c0 + u * 256) * 2);
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
+          for (int u = 0; u < U; ++u)
             if (c0 + u * 256 < H) acc8<T16>(acc[u], v[u]);
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < U; ++u) {
           const int c = c0 + u * 256;
           if (c >= H) continue;
           if (b0) acc8<T16>(acc[u], *reinterpret_cast<const int4*>(b0 + c));

@@ -80,6 +80,7 @@ void ll_combine_recv(SymmHeap& heap, const at::Tensor& topk_idx, const at::Tenso
 // diag.cu
 void device_barrier(SymmHeap& heap);
 void wait_probe(SymmHeap& heap, int64_t budget_ns);
+void fence_cost(SymmHeap& heap, int64_t peer, int64_t bytes, int64_t scope, at::Tensor out);
 
 // gemm.cu
 void grouped_gemm_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, const OptTensor& C,

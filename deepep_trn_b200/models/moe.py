@@ -15,6 +15,8 @@ grouped GEMM over the permuted activations.
 
 Weights: W1 [EL, 2I, H] with gate and up rows interleaved in 128-row blocks
 (``ops.gemm.interleave_gate_up``), W2 [EL, H, I], router Wr [E, H]; all bf16.
+Router logits come out of the same tensor-core GEMM with an fp32 epilogue, so
+expert selection matches an fp32 router up to summation order.
 """
 from __future__ import annotations
 
@@ -23,6 +25,23 @@ import torch.nn as nn
 
 from ..ops import gemm as G
 from ..ops import moe_ops as MO
+
+
+_OFFS: dict = {}
+
+
+def _single_segment(T: int, device) -> torch.Tensor:
+    """Offsets [0, T rounded up to 128] for one-group GEMMs (cached per size and device)."""
+    key = (T, str(device))
+    if key not in _OFFS:
+        _OFFS[key] = torch.tensor([0, (T + 127) // 128 * 128], dtype=torch.int64, device=device)
+    return _OFFS[key]
+
+
+def router_logits(x, Wr):
+    """fp32 logits [T, E] = x @ Wr^T on the tensor cores (bf16 inputs, fp32 accumulate and output)."""
+    return G.grouped_gemm(x.contiguous(), Wr.unsqueeze(0).contiguous(), _single_segment(x.shape[0], x.device),
+                          epilogue='f32')
 
 
 def _expert_forward(rows, offsets, W1, W2):
@@ -35,7 +54,7 @@ class _MoEFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, Wr, W1, W2, buf, num_experts, topk):
         EL = num_experts // buf.group_size
-        logits = (x @ Wr.t()).float()
+        logits = router_logits(x, Wr)
         idx, w = MO.router_topk(logits, topk)
         ntr, _, nte, itr, _ = buf.get_dispatch_layout(idx, num_experts)
         recv_x, recv_idx, recv_w, per_expert, handle, _ = buf.dispatch(
@@ -63,10 +82,12 @@ class _MoEFunction(torch.autograd.Function):
         dW1 = G.grouped_gemm_wgrad(MO.transpose(dpre), MO.transpose(rows), offsets, out_dtype=torch.float32)
         d_recv_x = MO.permute_bwd(drows, pos)
         dx, dw, _ = buf.combine(d_recv_x, handle, topk_weights=d_recv_w)   # dispatch backward
-        dlogits = MO.router_topk_bwd(idx, w, dw.float(), ctx.num_experts)
-        dx = (dx.float() + dlogits @ Wr.float()).to(x.dtype)
-        dWr = (dlogits.t() @ x.float()).to(Wr.dtype)
-        return dx, dWr, dW1.to(W1.dtype), dW2.to(W2.dtype), None, None, None
+        dlogits = MO.router_topk_bwd(idx, w, dw.float(), ctx.num_experts).to(x.dtype)
+        seg = _single_segment(x.shape[0], x.device)
+        dx_router = G.grouped_gemm(dlogits, MO.transpose(Wr).unsqueeze(0), seg, epilogue='f32')   # [T, H]
+        dx = (dx.float() + dx_router).to(x.dtype)
+        dWr = G.grouped_gemm_wgrad(MO.transpose(dlogits), MO.transpose(x), seg)[0]               # [E, H]
+        return dx, dWr.to(Wr.dtype), dW1.to(W1.dtype), dW2.to(W2.dtype), None, None, None
 
 
 class MoELayer(nn.Module):

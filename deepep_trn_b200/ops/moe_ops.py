@@ -72,7 +72,7 @@ def permute(x: torch.Tensor, local_ids: torch.Tensor, num_local_experts: int, co
     pos = torch.empty(N, K, dtype=torch.int32, device=dev)
     offsets = torch.empty(EL + 1, dtype=torch.int64, device=dev)
     cnt = torch.empty(EL, dtype=torch.int32, device=dev)
-    nblocks = max(1, (N + 255) // 256)
+    nblocks = max(1, (N + 31) // 32)
     scratch = torch.empty(nblocks * EL, dtype=torch.int32, device=dev)
     load().permute(x, local_ids.contiguous(), EL, rows, pos, offsets, cnt, scratch)
     return rows, pos, offsets, cnt

@@ -63,3 +63,13 @@ def test_low_latency_gloo(run_dist, ep):
     rc, out = run_dist('low_latency.py', 4, '--backend', 'gloo', '--ep', ep, '--hidden', 256, '--experts', 32,
                        '--topk', 4, timeout=600)
     assert rc == 0 and 'LOW_LATENCY_PASS' in out, out[-4000:]
+
+
+REF = __import__('pathlib').Path(__file__).resolve().parents[1] / 'baseline' / '_ref' / 'deep_ep_trn'
+
+
+@pytest.mark.skipif(not REF.exists(), reason='reference not installed under baseline/_ref')
+@pytest.mark.parametrize('nproc', [4, 2])
+def test_reference_parity_gloo(run_dist, nproc):
+    rc, out = run_dist('ref_parity.py', nproc, timeout=600)
+    assert rc == 0 and 'REF_PARITY_PASS' in out, out[-4000:]
