@@ -56,6 +56,7 @@ def parse():
     p.add_argument('--no-e2e', action='store_true')
     p.add_argument('--fp8', action='store_true', help='quantise to fp8 1x128 inside dispatch (config 3)')
     p.add_argument('--profile', action='store_true', help='print a per-kernel breakdown (torch.profiler) to stderr')
+    p.add_argument('--trace', action='store_true', help='print device phase timestamps of one step per rank')
     return p.parse_args()
 
 
@@ -159,6 +160,15 @@ def main():
 
     if args.profile:
         profile_steps(lambda: step(x, idx, w), 'normal d+c', rank)
+    if args.trace and args.impl == 'ours':
+        for _ in range(3):
+            step(x, idx, w)
+        tr = buf.device_trace()
+        everyone = [None] * world
+        dist.all_gather_object(everyone, (rank, tr), group=control)
+        if rank == 0:
+            for r, t in everyone:
+                log(f'device trace rank {r}: ' + ' '.join(f'{k}={v}' for k, v in t.items()))
 
     # ---- end to end through the public API: pinned H2D of inputs, D2H of the combined result
     e2e = None

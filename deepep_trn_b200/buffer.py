@@ -140,6 +140,10 @@ class Buffer:
     def clean_low_latency_buffer(self, *args, **kwargs) -> None:
         """No-op: flags are epoch-tagged, so low-latency buffers never need cleaning."""
 
+    def device_trace(self) -> dict:
+        """Per-phase device time (us) of the last normal-mode dispatch and combine (NVLink backend)."""
+        return self._engine.device_trace() if hasattr(self._engine, 'device_trace') else {}
+
     def check(self) -> None:
         """Raise if a kernel of this buffer reported a device-side error (timeouts, capacity)."""
         if hasattr(self._engine, 'check'):

@@ -21,6 +21,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("close", &SymmHeap::close)
       .def("status", &SymmHeap::status)
       .def("clear_status", &SymmHeap::clear_status)
+      .def("trace", &SymmHeap::trace)
       .def("wait_notify", &SymmHeap::wait_notify, py::call_guard<py::gil_scoped_release>())
       .def_property_readonly("rank", &SymmHeap::rank)
       .def_property_readonly("world", &SymmHeap::world)

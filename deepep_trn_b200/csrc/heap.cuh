@@ -15,6 +15,16 @@
 
 namespace b200ep {
 
+// Device trace points: the last op of each kind stamps %globaltimer at fixed phases.
+enum TracePoint : int {
+  kTrPrepStart = 0, kTrPrepScanDone, kTrPrepCopiesDone, kTrPrepPeersReady, kTrPrepNotified,
+  kTrPullStart = 8, kTrPullEnd,
+  kTrCombStart = 16, kTrCombPushDone, kTrCombPeersReady, kTrCombEnd,
+  kTrLLSendStart = 24, kTrLLSendEnd, kTrLLRecvStart, kTrLLRecvReady, kTrLLRecvEnd,
+  kTrLCSendStart = 32, kTrLCSendEnd, kTrLCRecvStart, kTrLCRecvReady, kTrLCRecvEnd,
+  kTracePoints = 40,
+};
+
 enum EpochId : int {
   kEpND = 0,    // normal dispatch (prepare kernel advances it)
   kEpNC = 1,    // normal combine
@@ -45,6 +55,8 @@ struct LocalState {
   int64_t nd_num_recv[2];
   uint32_t ll_expect[2][B200EP_MAX_RANKS];        // ll_cnt values already consumed
   uint32_t lc_expect[2][B200EP_MAX_RANKS];        // lc_cnt values already consumed
+  uint32_t arrive2[kNumEpochs];                   // second arrival counters (phase ends)
+  uint64_t trace[kTracePoints];                   // %globaltimer stamps of the last op of each kind
 };
 
 struct HeapConfig {

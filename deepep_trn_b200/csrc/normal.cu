@@ -18,12 +18,15 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstdlib>
+
 #include "ops.h"
 
 namespace b200ep {
 
 constexpr int kPrepThreads = 512;
 constexpr int kPrepMaxExperts = 8192;
+constexpr int kScanBytes = 16384;  // is_token_in_rank bytes staged per scan chunk
 constexpr int kPullThreads = 256;
 constexpr int kPullChunk = 256;
 constexpr int kCombThreads = 512;
@@ -83,6 +86,7 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
   if (T > M) {
     if (blockIdx.x == 0 && tid == 0) report_error(hv.status, kCapacity, 1, me, -1, M, T);
   }
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrPrepStart] = global_ns();
 
   // ---------------------------------------------------------------- CTA 0: per-destination scan
   // Each thread owns a contiguous chunk of tokens; one block-wide exclusive scan per
@@ -90,66 +94,81 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
   // in token order.
   if (blockIdx.x == 0) {
     const int Tc = min(T, M);
-    const int tpt = (Tc + kPrepThreads - 1) / kPrepThreads;
-    const int c0 = min(Tc, tid * tpt), c1 = min(Tc, c0 + tpt);
-    int cnt[B200EP_MAX_RANKS];
-#pragma unroll
-    for (int r = 0; r < B200EP_MAX_RANKS; ++r) cnt[r] = 0;
-    for (int t = c0; t < c1; ++t) {
-      const bool* row = a.in_rank + static_cast<int64_t>(t) * R;
-#pragma unroll
-      for (int r = 0; r < B200EP_MAX_RANKS; ++r)
-        if (r < R && row[r]) ++cnt[r];
-    }
-    // warp inclusive scans, then warp offsets
-    int incl[B200EP_MAX_RANKS];
-#pragma unroll
-    for (int r = 0; r < B200EP_MAX_RANKS; ++r) {
-      if (r >= R) continue;
-      int v = cnt[r];
-#pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const int u = __shfl_up_sync(0xffffffffu, v, d);
-        if (lane >= d) v += u;
+    __shared__ __align__(16) uint8_t s_mask[kScanBytes];
+    if (tid < R) s_base[tid] = 0;
+    const int TC = kScanBytes / R;  // tokens per chunk staged in shared memory
+    for (int cs = 0; cs < Tc; cs += TC) {
+      const int n = min(TC, Tc - cs);
+      const int nbytes = n * R;
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(a.in_rank) + static_cast<int64_t>(cs) * R;
+      if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        for (int i = tid; i < nbytes / 16; i += kPrepThreads)
+          reinterpret_cast<int4*>(s_mask)[i] = reinterpret_cast<const int4*>(src)[i];
+        for (int i = (nbytes / 16) * 16 + tid; i < nbytes; i += kPrepThreads) s_mask[i] = src[i];
+      } else {
+        for (int i = tid; i < nbytes; i += kPrepThreads) s_mask[i] = src[i];
       }
-      incl[r] = v;
-      if (lane == 31) s_cnt[r][warp] = v;
-    }
-    __syncthreads();
-    if (tid < R) {
-      int run = 0;
-      for (int w = 0; w < nwarps; ++w) {
-        const int c = s_cnt[tid][w];
-        s_cnt[tid][w] = run;
-        run += c;
-      }
-      s_base[tid] = run;  // total rows for destination tid
-    }
-    __syncthreads();
-    int off[B200EP_MAX_RANKS];
+      __syncthreads();
+      const int tpt = (n + kPrepThreads - 1) / kPrepThreads;
+      const int c0 = min(n, tid * tpt), c1 = min(n, c0 + tpt);
+      int cnt[B200EP_MAX_RANKS];
 #pragma unroll
-    for (int r = 0; r < B200EP_MAX_RANKS; ++r)
-      if (r < R) off[r] = s_cnt[r][warp] + incl[r] - cnt[r];
-    for (int t = c0; t < c1; ++t) {
-      const bool* row = a.in_rank + static_cast<int64_t>(t) * R;
-      int32_t* pos_row = a.token_pos + static_cast<int64_t>(t) * R;
+      for (int r = 0; r < B200EP_MAX_RANKS; ++r) cnt[r] = 0;
+      for (int t = c0; t < c1; ++t) {
+#pragma unroll
+        for (int r = 0; r < B200EP_MAX_RANKS; ++r)
+          if (r < R && s_mask[t * R + r]) ++cnt[r];
+      }
+      int incl[B200EP_MAX_RANKS];
 #pragma unroll
       for (int r = 0; r < B200EP_MAX_RANKS; ++r) {
         if (r >= R) continue;
-        if (row[r]) {
-          pos_row[r] = off[r];
-          stage_lists[static_cast<int64_t>(r) * M + off[r]] = t;
-          ++off[r];
-        } else {
-          pos_row[r] = -1;
+        int v = cnt[r];
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const int u = __shfl_up_sync(0xffffffffu, v, d);
+          if (lane >= d) v += u;
+        }
+        incl[r] = v;
+        if (lane == 31) s_cnt[r][warp] = v;
+      }
+      __syncthreads();
+      if (tid < R) {
+        int run = s_base[tid];
+        for (int w = 0; w < nwarps; ++w) {
+          const int c = s_cnt[tid][w];
+          s_cnt[tid][w] = run;
+          run += c;
+        }
+        s_base[tid] = run;  // rows for destination tid so far
+      }
+      __syncthreads();
+      int off[B200EP_MAX_RANKS];
+#pragma unroll
+      for (int r = 0; r < B200EP_MAX_RANKS; ++r)
+        if (r < R) off[r] = s_cnt[r][warp] + incl[r] - cnt[r];
+      for (int t = c0; t < c1; ++t) {
+        int32_t* pos_row = a.token_pos + static_cast<int64_t>(cs + t) * R;
+#pragma unroll
+        for (int r = 0; r < B200EP_MAX_RANKS; ++r) {
+          if (r >= R) continue;
+          if (s_mask[t * R + r]) {
+            pos_row[r] = off[r];
+            stage_lists[static_cast<int64_t>(r) * M + off[r]] = cs + t;
+            ++off[r];
+          } else {
+            pos_row[r] = -1;
+          }
         }
       }
+      __syncthreads();
     }
     int32_t* stage_counts = hv.at<int32_t>(me, hv.L.nd_counts[slot]);
     int32_t* stage_nte = hv.at<int32_t>(me, hv.L.nd_nte[slot]);
     if (tid < R) stage_counts[tid] = s_base[tid];
     if (a.has_nte)
       for (int i = tid; i < a.E; i += kPrepThreads) stage_nte[i] = a.nte[i];
+    if (tid == 0) ls->trace[kTrPrepScanDone] = global_ns();
   }
 
   // ---------------------------------------------------------------- copiers: stage rows + top-k
@@ -203,6 +222,7 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
   if (!s_last) return;
 
   // ---------------------------------------------------------------- last CTA: notify
+  if (tid == 0) ls->trace[kTrPrepCopiesDone] = global_ns();
   if (tid < R) {
     fence_sys();  // acquire side of the arrival counter, then release to the peer
     st_release_sys(&hv.sig(tid)->nd_ready[slot][me], e);
@@ -212,6 +232,7 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
       atomicExch(&s_fail, 1);
   }
   __syncthreads();
+  if (tid == 0) ls->trace[kTrPrepPeersReady] = global_ns();
   __shared__ int32_t s_rc[B200EP_MAX_RANKS];
   if (tid < R) {
     int32_t c = s_fail ? 0 : ld_volatile_i32(hv.at<int32_t>(tid, hv.L.nd_counts[slot]) + me);
@@ -251,6 +272,7 @@ __global__ void __launch_bounds__(kPrepThreads) nd_prepare_kernel(NdPrepArgs a) 
     ls->arrive[kEpND] = 0;
     __threadfence_system();
     st_release_sys64(const_cast<uint64_t*>(&host->notify.ticket), a.ticket);
+    ls->trace[kTrPrepNotified] = global_ns();
   }
 }
 
@@ -358,6 +380,7 @@ __global__ void __launch_bounds__(kPullThreads) nd_pull_kernel(NdPullArgs a) {
   __shared__ int32_t s_src[kPullChunk];
   __shared__ int32_t s_tok[kPullChunk];
   if (tid <= R) s_off[tid] = ls->nd_recv_off[slot][tid];
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrPullStart] = global_ns();
   __syncthreads();
   int64_t N = s_off[R];
   if (N > a.capacity) {
@@ -462,6 +485,12 @@ __global__ void __launch_bounds__(kPullThreads) nd_pull_kernel(NdPullArgs a) {
     __syncthreads();
   }
   if (a.use_tma && tid == 0) bulk_wait<0>();
+  // last CTA stamps the end of the pull
+  __syncthreads();
+  if (tid == 0 && atomicAdd(&ls->arrive2[kEpND], 1u) == gridDim.x - 1) {
+    ls->arrive2[kEpND] = 0;
+    ls->trace[kTrPullEnd] = global_ns();
+  }
 }
 
 void nd_pull(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_scales, const OptTensor& recv_topk,
@@ -542,6 +571,9 @@ struct NcArgs {
   const uint8_t* bias0;
   const uint8_t* bias1;
   int T, H, K;
+  int use_tma;            // rows of x are contiguous and 16-byte aligned: push with bulk copies
+  int chunk_bytes;        // bytes per bulk copy (multiple of 16)
+  int nstages;
 };
 
 template <typename T16>
@@ -567,18 +599,97 @@ __global__ void __launch_bounds__(kCombThreads) nc_combine_kernel(NcArgs a) {
   __shared__ int64_t s_off[B200EP_MAX_RANKS + 1];
   __shared__ int s_last, s_fail;
   if (tid <= R) s_off[tid] = a.recv_off[tid];
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrCombStart] = global_ns();
   __syncthreads();
   const int64_t N = s_off[R];
 
   // ---------------------------------------------------------------- push rows home
-  for (int64_t i = gw; i < N; i += GW) {
-    int s = 0;
-    while (s + 1 < R && s_off[s + 1] <= i) ++s;
-    const int64_t j = i - s_off[s];
-    if (j >= M || s == me) continue;  // own rows are read from x in place by the reduce
-    const int64_t slot_row = static_cast<int64_t>(me) * M + j;
-    warp_copy(hv.at<uint8_t>(s, hv.L.nc_rows[slot]) + slot_row * RB, a.x + i * a.x_stride, RB);
-    if (a.w && lane < K) hv.at<float>(s, hv.L.nc_w[slot])[slot_row * K + lane] = a.w[i * a.w_stride + lane];
+  // Rows from source s occupy x[off[s], off[s+1]) and land contiguously in s's return
+  // block [me][0, count), so each peer's share is one contiguous byte range.
+  if (a.use_tma) {
+    extern __shared__ __align__(1024) uint8_t smem_push[];
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_push + static_cast<int64_t>(a.nstages) * a.chunk_bytes);
+    // chunks of every peer's byte range, in rank order (own rows excluded); a peer's last
+    // chunk may be short, and no chunk spans two peers
+    int64_t nchunks = 0;
+    for (int s = 0; s < R; ++s)
+      if (s != me) nchunks += ((s_off[s + 1] - s_off[s]) * RB + a.chunk_bytes - 1) / a.chunk_bytes;
+    const int64_t c0 = nchunks * blockIdx.x / gridDim.x, c1 = nchunks * (blockIdx.x + 1) / gridDim.x;
+    if (tid == 0 && c1 > c0) {
+      for (int st = 0; st < a.nstages; ++st) mbar_init(&bars[st], 1);
+      fence_mbar_init();
+      auto locate = [&](int64_t c, const uint8_t*& src, uint8_t*& dst, uint32_t& bytes) {
+        for (int s = 0; s < R; ++s) {
+          if (s == me) continue;
+          const int64_t len = (s_off[s + 1] - s_off[s]) * RB;
+          const int64_t nc = (len + a.chunk_bytes - 1) / a.chunk_bytes;
+          if (c < nc) {
+            const int64_t byte = c * a.chunk_bytes;
+            src = a.x + s_off[s] * RB + byte;
+            dst = hv.at<uint8_t>(s, hv.L.nc_rows[slot]) + static_cast<int64_t>(me) * M * RB + byte;
+            bytes = static_cast<uint32_t>(len - byte < a.chunk_bytes ? len - byte : a.chunk_bytes);
+            return;
+          }
+          c -= nc;
+        }
+        bytes = 0;
+      };
+      uint32_t phase_bits = 0;
+      const int64_t n = c1 - c0;
+      auto issue = [&](int64_t q) {
+        const int st = static_cast<int>(q % a.nstages);
+        const uint8_t* src;
+        uint8_t* dst;
+        uint32_t bytes;
+        locate(c0 + q, src, dst, bytes);
+        mbar_arrive_expect_tx(&bars[st], bytes);
+        if (bytes) bulk_load(smem_push + static_cast<int64_t>(st) * a.chunk_bytes, src, bytes, &bars[st]);
+      };
+      const int64_t pro = n < a.nstages ? n : a.nstages;
+      for (int64_t q = 0; q < pro; ++q) issue(q);
+      for (int64_t m = 0; m < n; ++m) {
+        const int st = static_cast<int>(m % a.nstages);
+        if (!mbar_wait(&bars[st], (phase_bits >> st) & 1u, hv.timeout_ns)) {
+          report_error(hv.status, kTimeoutCombine, 3, me, -1, 0, 0, 1);
+          break;
+        }
+        phase_bits ^= 1u << st;
+        const uint8_t* src;
+        uint8_t* dst;
+        uint32_t bytes;
+        locate(c0 + m, src, dst, bytes);
+        if (bytes) bulk_store(dst, smem_push + static_cast<int64_t>(st) * a.chunk_bytes, bytes);
+        bulk_commit();
+        const int64_t q = m - 1 + a.nstages;
+        if (m >= 1 && q < n) {
+          bulk_wait_read<1>();
+          issue(q);
+        }
+      }
+      bulk_wait<0>();              // this CTA's peer writes are complete
+      fence_proxy_async_global();  // order them before the generic-proxy arrival below
+    }
+    // weights: small, plain stores
+    if (a.w) {
+      for (int64_t i = blockIdx.x * kCombThreads + tid; i < N * K; i += static_cast<int64_t>(gridDim.x) * kCombThreads) {
+        const int64_t row = i / K, k = i % K;
+        int s = 0;
+        while (s + 1 < R && s_off[s + 1] <= row) ++s;
+        if (s == me) continue;
+        const int64_t j = row - s_off[s];
+        hv.at<float>(s, hv.L.nc_w[slot])[(static_cast<int64_t>(me) * M + j) * K + k] = a.w[row * a.w_stride + k];
+      }
+    }
+  } else {
+    for (int64_t i = gw; i < N; i += GW) {
+      int s = 0;
+      while (s + 1 < R && s_off[s + 1] <= i) ++s;
+      const int64_t j = i - s_off[s];
+      if (j >= M || s == me) continue;  // own rows are read from x in place by the reduce
+      const int64_t slot_row = static_cast<int64_t>(me) * M + j;
+      warp_copy(hv.at<uint8_t>(s, hv.L.nc_rows[slot]) + slot_row * RB, a.x + i * a.x_stride, RB);
+      if (a.w && lane < K) hv.at<float>(s, hv.L.nc_w[slot])[slot_row * K + lane] = a.w[i * a.w_stride + lane];
+    }
   }
   __syncthreads();
   if (tid == 0) {
@@ -596,6 +707,7 @@ __global__ void __launch_bounds__(kCombThreads) nc_combine_kernel(NcArgs a) {
     if (tid == 0) {
       ls->arrive[kEpNC] = 0;
       ls->epoch[kEpNC] = e;
+      ls->trace[kTrCombPushDone] = global_ns();
     }
   }
 
@@ -606,6 +718,7 @@ __global__ void __launch_bounds__(kCombThreads) nc_combine_kernel(NcArgs a) {
   }
   __syncthreads();  // every thread reads rows whose flags threads < R acquired
   if (s_fail) return;
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrCombPeersReady] = global_ns();
   const uint8_t* rows = hv.at<uint8_t>(me, hv.L.nc_rows[slot]);
   const float* wrows = hv.at<float>(me, hv.L.nc_w[slot]);
   const bool vec = (H % 8) == 0;
@@ -683,6 +796,11 @@ __global__ void __launch_bounds__(kCombThreads) nc_combine_kernel(NcArgs a) {
     }
     __syncwarp();
   }
+  __syncthreads();
+  if (tid == 0 && atomicAdd(&ls->arrive2[kEpNC], 1u) == gridDim.x - 1) {
+    ls->arrive2[kEpNC] = 0;
+    ls->trace[kTrCombEnd] = global_ns();
+  }
 }
 
 void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const at::Tensor& recv_off,
@@ -725,12 +843,23 @@ void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const a
   int grid = num_sms > 0 ? static_cast<int>(num_sms) : heap.num_sms();
   void* kfn = x.scalar_type() == at::kHalf ? reinterpret_cast<void*>(nc_combine_kernel<__half>)
                                            : reinterpret_cast<void*>(nc_combine_kernel<__nv_bfloat16>);
+  const uintptr_t xp = reinterpret_cast<uintptr_t>(a.x);
+  a.use_tma = (xp & 15) == 0 && a.x_stride == 2LL * a.H && (a.x_stride % 16) == 0 && !getenv("B200EP_NO_TMA");
+  a.chunk_bytes = 16384;
+  a.nstages = 8;
+  const size_t smem = a.use_tma ? static_cast<size_t>(a.nstages) * a.chunk_bytes + a.nstages * 8 : 0;
+  static bool attr_set[2] = {false, false};
+  const int which = x.scalar_type() == at::kHalf ? 1 : 0;
+  if (!attr_set[which]) {
+    AT_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
+    attr_set[which] = true;
+  }
   int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kCombThreads, 0);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kCombThreads, smem);
   grid = std::max(1, std::min(grid, per_sm * heap.num_sms()));
   void* args[] = {&a};
   // cooperative: every CTA waits for the peers after its own pushes, so all CTAs must be resident
-  AT_CUDA_CHECK(cudaLaunchCooperativeKernel(kfn, dim3(grid), dim3(kCombThreads), args, 0,
+  AT_CUDA_CHECK(cudaLaunchCooperativeKernel(kfn, dim3(grid), dim3(kCombThreads), args, smem,
                                             at::cuda::getCurrentCUDAStream()));
 }
 

@@ -27,6 +27,7 @@ class SymmHeap {
   HeapView view() const;
   std::vector<int64_t> status() const;
   void clear_status();
+  std::vector<int64_t> trace() const;
   std::vector<int64_t> wait_notify(uint64_t ticket, int num_local_experts, double timeout_s) const;
 
   int rank() const { return rank_; }

@@ -108,6 +108,16 @@ std::vector<int64_t> SymmHeap::status() const {
 
 void SymmHeap::clear_status() { std::memset(&host_->status, 0, sizeof(Status)); }
 
+// Copy of the device trace stamps (synchronises the device).
+std::vector<int64_t> SymmHeap::trace() const {
+  std::vector<uint64_t> t(kTracePoints, 0);
+  B200EP_CUDA_CHECK(cudaSetDevice(device_));
+  B200EP_CUDA_CHECK(cudaDeviceSynchronize());
+  B200EP_CUDA_CHECK(cudaMemcpy(t.data(), static_cast<uint8_t*>(local_) + layout_.local + offsetof(LocalState, trace),
+                               sizeof(uint64_t) * kTracePoints, cudaMemcpyDeviceToHost));
+  return std::vector<int64_t>(t.begin(), t.end());
+}
+
 // Spin on the host-mapped notify page until the prepare kernel published `ticket`.
 // Returns {num_recv, recv_counts[R]..., per_expert[EL]...}; throws on timeout or
 // on a device-side error.

@@ -53,12 +53,14 @@ class NvlinkEngine:
         self._ll_pending = False
         self._lc_pending = False
         self.last_exchange = None
+        self._last_spec = None
+        self._spec_cache: dict = {}
         if spec_hint is not None:
             self._ensure(spec_hint)
 
     # ------------------------------------------------------------------ heap
     def _ensure(self, spec: HeapSpec) -> None:
-        if self.heap is not None and self.spec.covers(spec):
+        if self.heap is not None and (spec is self._last_spec or self.spec.covers(spec)):
             return
         new = spec if self.spec is None else self.spec.merge(spec)
         if self.heap is not None:
@@ -68,6 +70,7 @@ class NvlinkEngine:
             self.heap.close()
         self.heap = create_heap(self.group, new, self.timeout_s)
         self.spec = new
+        self._last_spec = None
 
     def check(self) -> None:
         """Raise if any kernel of this buffer reported a device-side error."""
@@ -78,6 +81,21 @@ class NvlinkEngine:
             self.heap.clear_status()
             raise DeviceError(f'{ERRORS.get(code, "device error")} (code={code} op={op} rank={rank} '
                               f'peer={peer} expected={expected} seen={seen} aux={aux})')
+
+    def device_trace(self) -> dict:
+        """Phase durations (us) of the last normal-mode dispatch / combine on this rank, from
+        %globaltimer stamps the kernels write into the heap (synchronises the device)."""
+        if self.heap is None:
+            return {}
+        t = self.heap.trace()
+
+        def d(a, b):
+            return round((t[b] - t[a]) / 1e3, 2) if t[a] and t[b] else None
+        return {'prepare.scan': d(0, 1), 'prepare.copies': d(0, 2), 'prepare.wait_peers': d(2, 3),
+                'prepare.notify': d(3, 4), 'prepare.total': d(0, 4), 'gap.prepare_to_pull': d(4, 8),
+                'pull': d(8, 9), 'gap.pull_to_combine': d(9, 16), 'combine.push': d(16, 17),
+                'combine.wait_peers': d(17, 18), 'combine.reduce': d(18, 19), 'combine.total': d(16, 19),
+                'step.prepare_to_combine_end': d(0, 19)}
 
     def barrier(self) -> None:
         """Device-side barrier over the EP group (epoch flags in peer memory, bounded wait)."""
@@ -106,8 +124,15 @@ class NvlinkEngine:
         return int(n or Buffer.num_sms or 0)
 
     def _spec(self, H, K, E, Mll=None) -> HeapSpec:
+        key = (H, K, E, Mll)
+        sp = self._spec_cache.get(key)
+        if sp is not None and self.spec is not None and self.spec.covers(sp):
+            self._last_spec = sp
+            return sp
         cur = self.spec
-        return HeapSpec(self.M, Mll if Mll is not None else (cur.max_ll_tokens if cur else 1), H, K, E)
+        sp = HeapSpec(self.M, Mll if Mll is not None else (cur.max_ll_tokens if cur else 1), H, K, E)
+        self._spec_cache[key] = sp
+        return sp
 
     # ------------------------------------------------------------------ layout
     def get_dispatch_layout(self, topk_idx, num_experts):
@@ -156,10 +181,10 @@ class NvlinkEngine:
         with timer.stage('prepare'):
             self.C.nd_prepare(self.heap, xt if not fp8_in else xt.view(torch.uint8),
                               x_scales, mode, bool(round_scale),
-                              None if cached else topk_idx.contiguous(),
-                              None if (cached or topk_weights is None) else topk_weights.float().contiguous(),
-                              None if cached else nte.to(torch.int32).contiguous(),
-                              itr.contiguous(), token_pos, recv_off, E, self.ticket, nsm)
+                              None if cached else _contig(topk_idx),
+                              None if (cached or topk_weights is None) else _contig(_f32(topk_weights)),
+                              None if cached else _contig(nte if nte.dtype == torch.int32 else nte.to(torch.int32)),
+                              _contig(itr), token_pos, recv_off, E, self.ticket, nsm)
         # Outputs are sized for the worst case (every peer sends its full capacity) so the pull
         # kernel can be queued before the host learns the receive size; the host then waits
         # on the notify ticket while the GPU is already pulling, and returns the first N rows.
@@ -231,7 +256,7 @@ class NvlinkEngine:
         b = [t.contiguous() for t in bias]
         with timer.stage('combine'):
             self.C.nc_combine(self.heap, x if x.stride(1) == 1 else x.contiguous(),
-                              topk_weights.float().contiguous() if topk_weights is not None else None,
+                              _contig(_f32(topk_weights)) if topk_weights is not None else None,
                               handle.recv_off, handle.token_pos, out, out_w,
                               b[0] if len(b) > 0 else None, b[1] if len(b) > 1 else None, self._sms(config))
         if out_w is not None and topk_weights.dtype != torch.float32:
@@ -322,6 +347,14 @@ class NvlinkEngine:
         else:
             recv()
         return result, EventOverlap(), hook
+
+
+def _contig(t):
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def _f32(t):
+    return t if t.dtype == torch.float32 else t.float()
 
 
 class _OneShot:
