@@ -108,3 +108,70 @@ void layout(const at::Tensor& topk_idx, int64_t num_experts, int64_t num_ranks, 
 }
 
 }  // namespace b200ep
+
+// ============================================================================ allocation-free variant
+// The same kernel with its scratch in a file-scope device array (see noalloc.h).
+#include <cstdio>
+#include <mutex>
+
+#include "noalloc.h"
+
+namespace b200ep {
+namespace {
+
+constexpr int kNoAllocScratch = B200EP_NOALLOC_MAX_RANKS + B200EP_NOALLOC_MAX_EXPERTS + 1;
+
+// [R + E] accumulators and one arrival counter; zero at load time and returned to zero
+// by the last CTA of every launch.
+__device__ __align__(256) int32_t g_layout_scratch[kNoAllocScratch];
+
+constexpr int kMaxDevices = 64;
+int32_t* g_scratch_ptr[kMaxDevices] = {};
+std::mutex g_scratch_mu;
+
+// Device address of the scratch array on the current device, looked up once per device.
+// In host code the symbol is only a host-side handle; the kernel needs this address.
+cudaError_t scratch_for_current_device(int32_t** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    err = cudaGetSymbolAddress(&p, g_layout_scratch);
+    if (err != cudaSuccess) return err;
+    // the accumulators must start at zero; every launch leaves them at zero again
+    err = cudaMemset(p, 0, sizeof(g_layout_scratch));
+    if (err != cudaSuccess) return err;
+    g_scratch_ptr[dev] = static_cast<int32_t*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace b200ep
+
+extern "C" int b200ep_dispatch_layout_noalloc(const int64_t* topk_idx, int num_tokens, int topk, int num_experts,
+                                              int num_ranks, int32_t* num_tokens_per_rank,
+                                              int32_t* num_tokens_per_expert, bool* is_token_in_rank,
+                                              cudaStream_t stream) {
+  using namespace b200ep;
+  if (num_tokens < 0 || topk < 0 || num_experts <= 0 || num_ranks < 1 || num_ranks > B200EP_NOALLOC_MAX_RANKS ||
+      num_experts > B200EP_NOALLOC_MAX_EXPERTS || num_experts % num_ranks != 0) {
+    std::fprintf(stderr,
+                 "b200ep_dispatch_layout_noalloc: sizes outside the compiled limits (num_tokens=%d topk=%d "
+                 "num_experts=%d (max %d, divisible by num_ranks) num_ranks=%d (1..%d))\n",
+                 num_tokens, topk, num_experts, B200EP_NOALLOC_MAX_EXPERTS, num_ranks, B200EP_NOALLOC_MAX_RANKS);
+    return B200EP_NOALLOC_TOO_LARGE;
+  }
+  int32_t* scratch = nullptr;
+  cudaError_t err = scratch_for_current_device(&scratch);
+  if (err != cudaSuccess) return static_cast<int>(err);
+  const int grid = num_tokens > 0 ? (num_tokens + kLayoutThreads - 1) / kLayoutThreads : 1;
+  layout_kernel<int64_t><<<grid, kLayoutThreads, 0, stream>>>(topk_idx, num_tokens, topk, num_experts, num_ranks,
+                                                              num_experts / num_ranks, num_tokens_per_rank,
+                                                              num_tokens_per_expert, is_token_in_rank, scratch);
+  return static_cast<int>(cudaGetLastError());
+}
