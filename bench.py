@@ -57,6 +57,7 @@ def parse():
     p.add_argument('--fp8', action='store_true', help='quantise to fp8 1x128 inside dispatch (config 3)')
     p.add_argument('--profile', action='store_true', help='print a per-kernel breakdown (torch.profiler) to stderr')
     p.add_argument('--trace', action='store_true', help='print device phase timestamps of one step per rank')
+    p.add_argument('--no-combine-weights', action='store_true', help='combine without the top-k weight channel')
     return p.parse_args()
 
 
@@ -126,7 +127,7 @@ def main():
         if use_fp8:
             from deepep_trn_b200.utils.codec import dequantize_fp8_1x128
             rx = dequantize_fp8_1x128(*rx).to(torch.bfloat16)
-        out, ow, _ = buf.combine(rx, handle, topk_weights=rw)
+        out, ow, _ = buf.combine(rx, handle, topk_weights=None if args.no_combine_weights else rw)
         return out, ow, handle, itr
 
     # ---- correctness gate: identity combine returns x * ranks_visited exactly

@@ -19,7 +19,7 @@ namespace b200ep {
 enum TracePoint : int {
   kTrPrepStart = 0, kTrPrepScanDone, kTrPrepCopiesDone, kTrPrepPeersReady, kTrPrepNotified,
   kTrPullStart = 8, kTrPullEnd,
-  kTrCombStart = 16, kTrCombPushDone, kTrCombPeersReady, kTrCombEnd,
+  kTrCombStart = 16, kTrCombPushDone, kTrCombPeersReady, kTrCombEnd,  // push done = rows staged (pull form)
   kTrLLSendStart = 24, kTrLLSendEnd, kTrLLRecvStart, kTrLLRecvReady, kTrLLRecvEnd,
   kTrLCSendStart = 32, kTrLCSendEnd, kTrLCRecvStart, kTrLCRecvReady, kTrLCRecvEnd,
   kTracePoints = 40,
@@ -73,8 +73,10 @@ struct HeapLayout {
   int64_t row_stride;      // bytes per staged row: align16(2H); fp8 rows use [H payload | H/32 scales]
   // normal dispatch staging (x2)
   int64_t nd_x[2], nd_topk[2], nd_w[2], nd_lists[2], nd_counts[2], nd_nte[2];
-  // normal combine receive (x2): [R][M] rows of 2H bytes, [R][M][K] weights
+  // normal combine receive (x2): [R][M] rows of 2H bytes, [R][M][K] weights (push form)
   int64_t nc_rows[2], nc_w[2];
+  // normal combine send (x2, pull form): [R*M] rows of 2H bytes, [R*M][K] weights, [R+1] offsets
+  int64_t nc_send[2], nc_send_w[2], nc_send_off[2];
   // low-latency dispatch receive (x2): [R][Mll] rows, [R][Mll][K] ids
   int64_t ll_rows[2], ll_ids[2];
   // low-latency combine receive (x2): [Mll][K] rows of 2H bytes
@@ -106,6 +108,11 @@ inline HeapLayout make_layout(const HeapConfig& c) {
   for (int b = 0; b < 2; ++b) {
     L.nc_rows[b] = take(int64_t(c.R) * c.M * 2LL * c.H);
     L.nc_w[b] = take(int64_t(c.R) * c.M * c.K * 4);
+  }
+  for (int b = 0; b < 2; ++b) {
+    L.nc_send[b] = take(int64_t(c.R) * c.M * 2LL * c.H);
+    L.nc_send_w[b] = take(int64_t(c.R) * c.M * c.K * 4);
+    L.nc_send_off[b] = take(int64_t(c.R + 1) * 8);
   }
   for (int b = 0; b < 2; ++b) {
     L.ll_rows[b] = take(int64_t(c.R) * c.Mll * L.row_stride);

@@ -803,6 +803,219 @@ __global__ void __launch_bounds__(kCombThreads) nc_combine_kernel(NcArgs a) {
   }
 }
 
+
+// ============================================================================ combine (pull form)
+// Each expert rank stages the rows its peers need in its own heap (a local copy) and
+// publishes its receive offsets; every source then streams its tokens' rows in with
+// TMA bulk loads (the faster NVLink direction on this fabric) through a shared-memory
+// ring and reduces them in fp32 as they arrive, adds the optional bias and casts once.
+struct NcPullArgs {
+  HeapView hv;
+  const uint8_t* x;
+  int64_t x_stride;     // bytes
+  const float* w;
+  int64_t w_stride;
+  const int64_t* recv_off;
+  const int32_t* token_pos;
+  uint8_t* out;
+  float* out_w;
+  const uint8_t* bias0;
+  const uint8_t* bias1;
+  int T, H, K;
+  int nstages, stage_bytes;
+};
+
+constexpr int kPullTok = 16;   // tokens per batch (one warp builds each token's row list)
+
+template <typename T16>
+__global__ void __launch_bounds__(kCombThreads) nc_pull_kernel(NcPullArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_ring[];
+  const HeapView& hv = a.hv;
+  LocalState* ls = hv.local();
+  const uint32_t e = ld_volatile_u32(&ls->epoch[kEpNC]) + 1u;
+  const int slot = e & 1u;
+  const int me = hv.rank, R = hv.R;
+  const int H = a.H, K = a.K;
+  const int64_t RB = 2LL * H;
+  const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
+  constexpr int nwarps = kCombThreads / 32;
+  const int gw = blockIdx.x * nwarps + warp, GW = gridDim.x * nwarps;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_ring + static_cast<int64_t>(a.nstages) * a.stage_bytes);
+
+  __shared__ int64_t s_off[B200EP_MAX_RANKS + 1];
+  __shared__ int64_t s_roff[B200EP_MAX_RANKS];
+  __shared__ int s_last, s_fail;
+  __shared__ const uint8_t* s_src[kPullTok * B200EP_MAX_RANKS];
+  __shared__ int16_t s_n[kPullTok + 1];
+  if (tid <= R) s_off[tid] = a.recv_off[tid];
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrCombStart] = global_ns();
+  __syncthreads();
+  const int64_t N = s_off[R];
+
+  // ---------------------------------------------------------------- stage rows for the peers
+  uint8_t* send = hv.at<uint8_t>(me, hv.L.nc_send[slot]);
+  float* send_w = hv.at<float>(me, hv.L.nc_send_w[slot]);
+  for (int64_t i = gw; i < N; i += GW) {
+    if (i >= s_off[me] && i < s_off[me + 1]) continue;  // own rows are read in place
+    warp_copy(send + i * RB, a.x + i * a.x_stride, RB);
+    if (a.w && lane < K) send_w[i * K + lane] = a.w[i * a.w_stride + lane];
+  }
+  if (blockIdx.x == 0 && tid <= R) hv.at<int64_t>(me, hv.L.nc_send_off[slot])[tid] = s_off[tid];
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();  // local data; peers read it after the last CTA's system-scope release
+    s_last = atomicAdd(&ls->arrive[kEpNC], 1u) == gridDim.x - 1;
+    s_fail = 0;
+  }
+  __syncthreads();
+  if (s_last) {
+    if (tid < R) {
+      fence_sys();
+      st_release_sys(&hv.sig(tid)->nc_ready[slot][me], e);
+    }
+    if (tid == 0) {
+      ls->arrive[kEpNC] = 0;
+      ls->epoch[kEpNC] = e;
+      ls->trace[kTrCombPushDone] = global_ns();
+    }
+  }
+  // ---------------------------------------------------------------- wait for every expert rank
+  if (tid < R) {
+    if (!wait_epoch(&hv.sig(me)->nc_ready[slot][tid], e, hv.timeout_ns, hv.status, kTimeoutCombine, 3, me, tid))
+      s_fail = 1;
+    else
+      s_roff[tid] = tid == me ? s_off[me] : *reinterpret_cast<const volatile int64_t*>(
+                                                 hv.at<int64_t>(tid, hv.L.nc_send_off[slot]) + me);
+  }
+  __syncthreads();
+  if (s_fail) return;
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrCombPeersReady] = global_ns();
+  if (tid == 0) {
+    for (int st = 0; st < a.nstages; ++st) mbar_init(&bars[st], 1);
+    fence_mbar_init();
+    fence_proxy_async_global();
+  }
+  __syncthreads();
+
+  // ---------------------------------------------------------------- row stream + reduce
+  const int nch = H / 8;                           // 16-byte chunks per row
+  const int t0 = static_cast<int>(static_cast<int64_t>(a.T) * blockIdx.x / gridDim.x);
+  const int t1 = static_cast<int>(static_cast<int64_t>(a.T) * (blockIdx.x + 1) / gridDim.x);
+  uint32_t g = 0;  // rows consumed so far by this CTA (drives stage and parity)
+  for (int tb = t0; tb < t1; tb += kPullTok) {
+    const int nt = min(kPullTok, t1 - tb);
+    // row list of the batch, in (token, rank) order
+    if (warp < nt) {
+      const int t = tb + warp;
+      const int p = lane < R ? a.token_pos[static_cast<int64_t>(t) * R + lane] : -1;
+      const uint32_t b = __ballot_sync(0xffffffffu, p >= 0);
+      if (lane == 0) s_n[warp + 1] = static_cast<int16_t>(__popc(b));
+      __syncwarp();
+      if (p >= 0) {
+        const int q = __popc(b & lanemask_lt());
+        s_src[warp * B200EP_MAX_RANKS + q] =
+            lane == me ? a.x + (s_off[me] + p) * a.x_stride
+                       : hv.base[lane] + hv.L.nc_send[slot] + (s_roff[lane] + p) * RB;
+      }
+      if (a.out_w) {
+        // combined weights: sum over the ranks the token visited
+        float acc_w = 0.f;
+        for (int r = 0; r < R; ++r) {
+          const int pr = __shfl_sync(0xffffffffu, p, r);
+          if (pr < 0 || lane >= K) continue;
+          acc_w += r == me ? a.w[(s_off[me] + pr) * a.w_stride + lane]
+                           : *reinterpret_cast<const volatile float*>(
+                                 hv.at<float>(r, hv.L.nc_send_w[slot]) + (s_roff[r] + pr) * K + lane);
+        }
+        if (lane < K) a.out_w[static_cast<int64_t>(t) * K + lane] = acc_w;
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      s_n[0] = 0;
+      for (int i = 0; i < nt; ++i) s_n[i + 1] = static_cast<int16_t>(s_n[i] + s_n[i + 1]);
+    }
+    __syncthreads();
+    const int nrows = s_n[nt];
+    // compact the list: rows of token i sit at [s_n[i], s_n[i+1])
+    auto row_src = [&](int k) -> const uint8_t* {
+      int i = 0;
+      while (s_n[i + 1] <= k) ++i;
+      return s_src[i * B200EP_MAX_RANKS + (k - s_n[i])];
+    };
+    auto issue = [&](int k, uint32_t gk) {
+      const int st = static_cast<int>(gk % a.nstages);
+      mbar_arrive_expect_tx(&bars[st], static_cast<uint32_t>(RB));
+      bulk_load(smem_ring + static_cast<int64_t>(st) * a.stage_bytes, row_src(k), static_cast<uint32_t>(RB), &bars[st]);
+    };
+    if (tid == 0)
+      for (int k = 0; k < nrows && k < a.nstages; ++k) issue(k, g + k);
+    float acc[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[u][i] = 0.f;
+    int tok = 0;
+    for (int k = 0; k < nrows; ++k, ++g) {
+      const int st = static_cast<int>(g % a.nstages);
+      if (!mbar_wait(&bars[st], (g / a.nstages) & 1u, hv.timeout_ns)) {
+        if (tid == 0) report_error(hv.status, kTimeoutCombine, 3, me, -1, 0, 0, 2);
+        return;
+      }
+      const uint8_t* row = smem_ring + static_cast<int64_t>(st) * a.stage_bytes;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = tid + u * kCombThreads;
+        if (j < nch) acc8<T16>(acc[u], *reinterpret_cast<const int4*>(row + j * 16));
+      }
+      while (s_n[tok + 1] <= k) ++tok;
+      if (k + 1 == s_n[tok + 1]) {
+        // last row of this token: bias, cast, store, reset
+        const int64_t t = tb + tok;
+        T16* out = reinterpret_cast<T16*>(a.out) + t * H;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = tid + u * kCombThreads;
+          if (j >= nch) continue;
+          if (a.bias0) acc8<T16>(acc[u], reinterpret_cast<const int4*>(a.bias0 + t * RB)[j]);
+          if (a.bias1) acc8<T16>(acc[u], reinterpret_cast<const int4*>(a.bias1 + t * RB)[j]);
+          int4 o;
+          T16* oh = reinterpret_cast<T16*>(&o);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) oh[i] = static_cast<T16>(acc[u][i]);
+          reinterpret_cast<int4*>(out)[j] = o;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[u][i] = 0.f;
+        }
+      }
+      __syncthreads();  // every thread is done with stage st
+      if (tid == 0 && k + a.nstages < nrows) issue(k + a.nstages, g + a.nstages);
+    }
+    // tokens routed nowhere (all top-k masked) still get bias (or zeros)
+    for (int i = warp; i < nt; i += nwarps) {
+      if (s_n[i + 1] != s_n[i]) continue;
+      const int64_t t = tb + i;
+      T16* out = reinterpret_cast<T16*>(a.out) + t * H;
+      for (int j = lane; j < nch; j += 32) {
+        float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (a.bias0) acc8<T16>(z, reinterpret_cast<const int4*>(a.bias0 + t * RB)[j]);
+        if (a.bias1) acc8<T16>(z, reinterpret_cast<const int4*>(a.bias1 + t * RB)[j]);
+        int4 o;
+        T16* oh = reinterpret_cast<T16*>(&o);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) oh[q] = static_cast<T16>(z[q]);
+        reinterpret_cast<int4*>(out)[j] = o;
+      }
+    }
+    __syncthreads();
+  }
+  __syncthreads();
+  if (tid == 0 && atomicAdd(&ls->arrive2[kEpNC], 1u) == gridDim.x - 1) {
+    ls->arrive2[kEpNC] = 0;
+    ls->trace[kTrCombEnd] = global_ns();
+  }
+}
+
 void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const at::Tensor& recv_off,
                 const at::Tensor& token_pos, at::Tensor out, const OptTensor& out_w, const OptTensor& bias0,
                 const OptTensor& bias1, int64_t num_sms) {
@@ -844,9 +1057,49 @@ void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const a
   void* kfn = x.scalar_type() == at::kHalf ? reinterpret_cast<void*>(nc_combine_kernel<__half>)
                                            : reinterpret_cast<void*>(nc_combine_kernel<__nv_bfloat16>);
   const uintptr_t xp = reinterpret_cast<uintptr_t>(a.x);
+  const bool aligned = (xp & 15) == 0 && (a.x_stride % 16) == 0 && (a.H % 8) == 0 && a.H <= 4 * 8 * kCombThreads;
+  if (aligned && !getenv("B200EP_COMBINE_PUSH")) {
+    NcPullArgs p{};
+    p.hv = a.hv;
+    p.x = a.x;
+    p.x_stride = a.x_stride;
+    p.w = a.w;
+    p.w_stride = a.w_stride;
+    p.recv_off = a.recv_off;
+    p.token_pos = a.token_pos;
+    p.out = a.out;
+    p.out_w = a.out_w;
+    p.bias0 = a.bias0;
+    p.bias1 = a.bias1;
+    p.T = a.T;
+    p.H = a.H;
+    p.K = a.K;
+    p.stage_bytes = static_cast<int>(align_up(2LL * a.H, 128));
+    p.nstages = static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(12, (176 * 1024) / p.stage_bytes)));
+    const size_t psmem = static_cast<size_t>(p.nstages) * p.stage_bytes + p.nstages * 8;
+    void* pfn = x.scalar_type() == at::kHalf ? reinterpret_cast<void*>(nc_pull_kernel<__half>)
+                                             : reinterpret_cast<void*>(nc_pull_kernel<__nv_bfloat16>);
+    static bool pattr[2] = {false, false};
+    const int pw = x.scalar_type() == at::kHalf ? 1 : 0;
+    if (!pattr[pw]) {
+      AT_CUDA_CHECK(cudaFuncSetAttribute(pfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+      pattr[pw] = true;
+    }
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pfn, kCombThreads, psmem);
+    const int g = std::max(1, std::min(grid, per_sm * heap.num_sms()));
+    void* pargs[] = {&p};
+    // cooperative: every CTA waits for the other ranks after staging, so all CTAs must be resident
+    AT_CUDA_CHECK(cudaLaunchCooperativeKernel(pfn, dim3(g), dim3(kCombThreads), pargs, psmem,
+                                              at::cuda::getCurrentCUDAStream()));
+    return;
+  }
   a.use_tma = (xp & 15) == 0 && a.x_stride == 2LL * a.H && (a.x_stride % 16) == 0 && !getenv("B200EP_NO_TMA");
   a.chunk_bytes = 16384;
   a.nstages = 8;
+  if (const char* v = getenv("B200EP_PUSH_CHUNK")) a.chunk_bytes = std::max(1024, atoi(v)) / 16 * 16;
+  if (const char* v = getenv("B200EP_PUSH_STAGES")) a.nstages = std::max(2, std::min(16, atoi(v)));
+  while (static_cast<int64_t>(a.nstages) * a.chunk_bytes > 150 * 1024 && a.nstages > 2) --a.nstages;
   const size_t smem = a.use_tma ? static_cast<size_t>(a.nstages) * a.chunk_bytes + a.nstages * 8 : 0;
   static bool attr_set[2] = {false, false};
   const int which = x.scalar_type() == at::kHalf ? 1 : 0;
