@@ -52,9 +52,11 @@ def _expert_forward(rows, offsets, W1, W2):
 
 class _MoEFunction(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, Wr, W1, W2, buf, num_experts, topk):
+    def forward(ctx, x, Wr, W1, W2, buf, num_experts, topk, router_bias=None):
         EL = num_experts // buf.group_size
         logits = router_logits(x, Wr)
+        if router_bias is not None:
+            logits = logits + router_bias
         idx, w = MO.router_topk(logits, topk)
         ntr, _, nte, itr, _ = buf.get_dispatch_layout(idx, num_experts)
         recv_x, recv_idx, recv_w, per_expert, handle, _ = buf.dispatch(
@@ -87,7 +89,7 @@ class _MoEFunction(torch.autograd.Function):
         dx_router = G.grouped_gemm(dlogits, MO.transpose(Wr).unsqueeze(0), seg, epilogue='f32')   # [T, H]
         dx = (dx.float() + dx_router).to(x.dtype)
         dWr = G.grouped_gemm_wgrad(MO.transpose(dlogits), MO.transpose(x), seg)[0]               # [E, H]
-        return dx, dWr.to(Wr.dtype), dW1.to(W1.dtype), dW2.to(W2.dtype), None, None, None
+        return dx, dWr.to(Wr.dtype), dW1.to(W1.dtype), dW2.to(W2.dtype), None, None, None, None
 
 
 class MoELayer(nn.Module):
@@ -113,14 +115,20 @@ class MoELayer(nn.Module):
         wu = torch.randn(EL, intermediate, hidden, generator=g_local) * std
         self.w1 = nn.Parameter(G.interleave_gate_up(wg, wu).to(dtype).to(device))
         self.w2 = nn.Parameter((torch.randn(EL, hidden, intermediate, generator=g_local) * std).to(dtype).to(device))
+        # fp32 bias added to the router logits before top-k (not trained here; it steers load,
+        # e.g. a Zipf skew for benchmarks or a balancing bias)
+        self.register_buffer('router_bias', torch.zeros(num_experts, dtype=torch.float32, device=device))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return _MoEFunction.apply(x, self.router, self.w1, self.w2, self.buffer, self.num_experts, self.topk)
+        return _MoEFunction.apply(x, self.router, self.w1, self.w2, self.buffer, self.num_experts, self.topk,
+                                  self.router_bias)
 
 
-def reference_moe(x, Wr, W1, W2, topk):
+def reference_moe(x, Wr, W1, W2, topk, router_bias=None):
     """fp32 torch definition of the layer on one rank holding all experts (W1 interleaved)."""
     logits = x.float() @ Wr.float().t()
+    if router_bias is not None:
+        logits = logits + router_bias
     idx, w = MO.router_topk(logits.cpu(), topk)
     idx, w = idx.to(x.device), w.to(x.device)
     out = torch.zeros(x.shape, dtype=torch.float32, device=x.device)
