@@ -64,10 +64,24 @@ def main():
     ms = timed(lambda: G.grouped_gemm(h, W2, offs, out=out), args.iters, flush)
     res['gemm2'] = dict(ms=round(ms, 4), tflops=round(f2 / ms / 1e9, 1))
     dO = (torch.randn(rows, H, device=dev) * 0.1).to(torch.bfloat16)
+    # backward shapes, operands read in place (MN-major): dX = dO @ W2, dW2 = dO^T @ h
+    dh = torch.empty(rows, I, device=dev, dtype=torch.bfloat16)
+    ms = timed(lambda: G.grouped_gemm(dO, W2, offs, out=dh, b_layout='kn'), args.iters, flush)
+    res['dgrad2_kn'] = dict(ms=round(ms, 4), tflops=round(f2 / ms / 1e9, 1))
+    dpre = (torch.randn(rows, 2 * I, device=dev) * 0.1).to(torch.bfloat16)
+    dA = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
+    ms = timed(lambda: G.grouped_gemm(dpre, W1, offs, out=dA, b_layout='kn'), args.iters, flush)
+    res['dgrad1_kn'] = dict(ms=round(ms, 4), tflops=round(f1 / ms / 1e9, 1))
+    dW2 = torch.empty(E, H, I, device=dev, dtype=torch.bfloat16)
+    ms = timed(lambda: G.grouped_gemm_wgrad(dO, h, offs, out=dW2), args.iters, flush)
+    res['wgrad2_tok'] = dict(ms=round(ms, 4), tflops=round(f2 / ms / 1e9, 1))
+    dW1 = torch.empty(E, 2 * I, H, device=dev, dtype=torch.bfloat16)
+    ms = timed(lambda: G.grouped_gemm_wgrad(dpre, A, offs, out=dW1), args.iters, flush)
+    res['wgrad1_tok'] = dict(ms=round(ms, 4), tflops=round(f1 / ms / 1e9, 1))
     dOt, ht = dO.t().contiguous(), h.t().contiguous()
-    dW2 = torch.empty(E, H, I, device=dev, dtype=torch.float32)
-    ms = timed(lambda: G.grouped_gemm_wgrad(dOt, ht, offs, out=dW2), args.iters, flush)
-    res['wgrad2'] = dict(ms=round(ms, 4), tflops=round(f2 / ms / 1e9, 1))
+    dW2f = torch.empty(E, H, I, device=dev, dtype=torch.float32)
+    ms = timed(lambda: G.grouped_gemm_wgrad(dOt, ht, offs, out=dW2f, layout='mk'), args.iters, flush)
+    res['wgrad2_mk_f32'] = dict(ms=round(ms, 4), tflops=round(f2 / ms / 1e9, 1))
     G.check()
     if not args.no_cublas:
         def cublas1():

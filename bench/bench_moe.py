@@ -33,6 +33,7 @@ def main():
     p.add_argument('--topk', type=int, default=8)
     p.add_argument('--steps', type=int, default=5)
     p.add_argument('--impls', default='ours,nccl')
+    p.add_argument('--breakdown', action='store_true', help='per-phase device time of the fused layer')
     p.set_defaults(tokens=[4096])
     args = p.parse_args()
     T = args.tokens[0]
@@ -86,6 +87,17 @@ def main():
         flops = 18.0 * T * K * H * I  # expert GEMMs per rank on average: forward 6*P*H*I, backward twice that
         results[impl] = dict(ms_per_step=round(ms, 3), tokens_per_s=round(T * ctx.ep / (ms * 1e-3), 1),
                              expert_tflops_per_rank=round(flops / (ms * 1e-3) / 1e12, 1))
+        if args.breakdown and impl == 'ours':
+            from deepep_trn_b200.utils.profiling import timer
+            timer.reset()
+            timer.enabled, timer.use_cuda_events = True, True
+            for _ in range(3):
+                step()
+            torch.cuda.synchronize()
+            per = timer.per_call_us(3)
+            timer.enabled = False
+            allr = ctx.gather({k: round(v, 1) for k, v in per.items() if k.startswith('moe.')})
+            results[impl]['breakdown_us'] = {k: [r[k] for r in allr] for k in allr[0]}
         buf.destroy()
         del layer
         torch.cuda.empty_cache()

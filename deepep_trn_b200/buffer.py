@@ -35,6 +35,22 @@ from .parallel.transport import GlooTransport, NcclTransport, Transport
 __all__ = ['Buffer', 'Config', 'DispatchHandle', 'EventOverlap', 'LowLatencyHandle']
 
 
+def check_agreement(group, config: dict) -> None:
+    """Raise ``ValueError`` on every rank if the ranks of ``group`` were given different ``config``.
+
+    One all-gather at construction; a mismatch (say, ranks sized for different token
+    capacities) would otherwise surface later as a capacity error or a timed-out wait
+    on one rank only.
+    """
+    world = dist.get_world_size(group)
+    seen = [None] * world
+    dist.all_gather_object(seen, config, group=group)
+    diff = {k: {r: c.get(k) for r, c in enumerate(seen)} for k in config
+            if len({repr(c.get(k)) for c in seen}) > 1}
+    if diff:
+        raise ValueError(f'Buffer configuration differs across the ranks of the group: {diff}')
+
+
 def _default_timeout() -> float:
     return float(os.environ.get('B200EP_TIMEOUT_S', '10'))
 
@@ -78,7 +94,13 @@ class Buffer:
                 raise ValueError(f'replica group {mine[0]} does not match the EP group {ranks}')
         if backend == 'auto':
             backend = 'nvlink' if (transport is None and torch.cuda.is_available()) else 'gloo'
+        if backend not in ('nvlink', 'gloo', 'nccl'):
+            raise ValueError(f'unknown backend {backend!r}')
         self.backend = backend
+        if world > 1:
+            check_agreement(group, dict(backend=backend, num_max_tokens_per_rank=self.num_max_tokens_per_rank,
+                                        num_max_dispatch_tokens_per_rank=num_max_dispatch_tokens_per_rank,
+                                        hidden=hidden, num_experts=num_experts, topk=topk))
         self.timeout_s = timeout_s if timeout_s is not None else _default_timeout()
         self.comm_stream = torch.cuda.Stream() if torch.cuda.is_available() and backend != 'gloo' else None
         self._last_event = None

@@ -3,7 +3,11 @@
 //   GROUP_M:  C[off_e : off_e+m_e, :] = A[off_e : off_e+m_e, :] @ B[e]^T      (forward, dX)
 //   GROUP_K:  C[e] = A[:, off_e : off_e+m_e] @ B[:, off_e : off_e+m_e]^T          (dW)
 //
-// A, B are bf16 and K-major (the reduction dimension is contiguous). Expert
+// A, B are bf16, each either K-major (the reduction dimension is contiguous) or
+// MN-major (the output dimension is contiguous), so transposed operands are read
+// in place instead of being materialised: the backward's dX GEMM takes the
+// forward weight [G, K, N] as an MN-major B, and the weight-gradient GEMM takes
+// the activations [tokens, M] and [tokens, N] as MN-major A and B. Expert
 // segments are padded to multiples of 128 rows (the permute kernel does this),
 // so every M tile (GROUP_M) or K block (GROUP_K) lies inside one expert.
 //
@@ -56,6 +60,14 @@ __device__ __forceinline__ void tma_load_2d(void* smem, const CUtensorMap* map, 
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
       ::"r"(smem_u32(smem)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void* smem, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(smem)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
@@ -112,10 +124,25 @@ __device__ __forceinline__ uint64_t smem_desc_k128(const void* p) {
   d |= 2ull << 61;                         // SWIZZLE_128B
   return d;
 }
-// Instruction descriptor: D fp32, A/B bf16, both K-major, M=128, N=n.
-__host__ __device__ constexpr uint32_t idesc_bf16(int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+// MN-major, 128-byte swizzle: each 128-byte row holds 64 consecutive M (or N) elements
+// of one k, 8 k-rows form a 1024-byte swizzle atom (stride byte offset), and the
+// 64-wide MN atoms of a tile sit `mn_atom_bytes` apart (leading byte offset). This is
+// what a SWIZZLE_128B TMA box of 64 (MN) x BK (K) elements produces, one box per atom.
+__device__ __forceinline__ uint64_t smem_desc_mn128(const void* p, uint32_t mn_atom_bytes) {
+  const uint64_t addr = smem_u32(p);
+  uint64_t d = (addr >> 4) & 0x3FFFull;
+  d |= static_cast<uint64_t>((mn_atom_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (1024ull >> 4) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
 }
+// Instruction descriptor: D fp32, A/B bf16, M=128, N=n; bits 15 / 16 select MN-major A / B.
+__host__ __device__ constexpr uint32_t idesc_bf16(int n, bool a_mn = false, bool b_mn = false) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(a_mn) << 15) | (uint32_t(b_mn) << 16) |
+         (uint32_t(n >> 3) << 17) | (uint32_t(BM >> 4) << 24);
+}
+constexpr uint32_t kMnAtomBytes = 64 * BK * 2;  // one 64-wide MN column of a BK-deep stage
 
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const Args& a) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -178,11 +205,14 @@ __device__ __forceinline__ bool tile_of(int t, const Args& a, const int64_t* off
   return true;
 }
 
-template <bool GROUP_K, int BN, int STAGES, int EPI>
+// LAYOUT bit 0: A is MN-major; bit 1: B is MN-major (GROUP_M: B is [G, K, N], read
+// through a 3-D map so a K tail never reaches into the next expert's weight).
+template <bool GROUP_K, int BN, int STAGES, int EPI, int LAYOUT>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   using S = Smem<BN>;
+  constexpr bool A_MN = (LAYOUT & 1) != 0, B_MN = (LAYOUT & 2) != 0;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::kABytes;
@@ -229,12 +259,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!wait_bar(&empty[s], ((it / STAGES) & 1u) ^ 1u, a)) { s_abort = 1; break; }
           mbar_arrive_expect_tx(&full[s], S::kStageBytes);
           const int kc = (tl.kb0 + kb) * BK;
-          if (!GROUP_K) {
-            tma_load_2d(sA + s * S::kABytes, &tmA, &full[s], kc, tl.m0);
-            tma_load_2d(sB + s * S::kBBytes, &tmB, &full[s], kc, tl.g * a.N + tl.n0);
+          uint8_t* da = sA + s * S::kABytes;
+          uint8_t* db = sB + s * S::kBBytes;
+          if (A_MN) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(da + j * kMnAtomBytes, &tmA, &full[s], tl.m0 + 64 * j, kc);
           } else {
-            tma_load_2d(sA + s * S::kABytes, &tmA, &full[s], kc, tl.m0);
-            tma_load_2d(sB + s * S::kBBytes, &tmB, &full[s], kc, tl.n0);
+            tma_load_2d(da, &tmA, &full[s], kc, tl.m0);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) {
+              if (!GROUP_K) tma_load_3d(db + j * kMnAtomBytes, &tmB, &full[s], tl.n0 + 64 * j, kc, tl.g);
+              else tma_load_2d(db + j * kMnAtomBytes, &tmB, &full[s], tl.n0 + 64 * j, kc);
+            }
+          } else {
+            tma_load_2d(db, &tmB, &full[s], kc, GROUP_K ? tl.n0 : tl.g * a.N + tl.n0);
           }
         }
       }
@@ -242,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(BN);
+      constexpr uint32_t idesc = idesc_bf16(BN, A_MN, B_MN);
       uint32_t it = 0, acc = 0;
       Tile tl;
       for (int t = blockIdx.x; tile_of<GROUP_K, BN>(t, a, s_offs, tl) && !s_abort; t += gridDim.x) {
@@ -256,13 +296,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int s = it % STAGES;
           if (!wait_bar(&full[s], (it / STAGES) & 1u, a)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t ad = smem_desc_k128(sA + s * S::kABytes);
-          const uint64_t bd = smem_desc_k128(sB + s * S::kBBytes);
+          const uint64_t ad = A_MN ? smem_desc_mn128(sA + s * S::kABytes, kMnAtomBytes)
+                                   : smem_desc_k128(sA + s * S::kABytes);
+          const uint64_t bd = B_MN ? smem_desc_mn128(sB + s * S::kBBytes, kMnAtomBytes)
+                                   : smem_desc_k128(sB + s * S::kBBytes);
+          // next 16-wide k slice: K-major advances 32 bytes inside the swizzle row (2 units),
+          // MN-major advances 16 rows of 128 bytes (128 units)
+          constexpr uint64_t astep = A_MN ? 128 : 2, bstep = B_MN ? 128 : 2;
 #pragma unroll
-          for (int k = 0; k < BK / UMMA_K; ++k) {
-            // advance 16 elements (32 bytes = 2 descriptor units) inside the swizzle row
-            tc_mma(dcol, ad + 2 * k, bd + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          }
+          for (int k = 0; k < BK / UMMA_K; ++k)
+            tc_mma(dcol, ad + astep * k, bd + bstep * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
           tc_commit(&empty[s]);
         }
         if (!ok) { s_abort = 1; break; }
@@ -402,10 +445,27 @@ CUtensorMap make_map(const void* base, int64_t rows, int64_t cols, int64_t ld, i
   return m;
 }
 
-template <bool GROUP_K, int BN, int STAGES, int EPI>
+// 3-D bf16 [G, K, N] (N contiguous): boxes of 64 (N) x BK (K) x 1, 128B swizzle. K past the
+// end of one group reads as zeros instead of the next group's first rows.
+CUtensorMap make_map_kn(const void* base, int64_t G, int64_t K, int64_t N) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((N * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(G)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(N * 2), static_cast<cuuint64_t>(K * N * 2)};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(BK), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (3-D) failed: ", static_cast<int>(r));
+  return m;
+}
+
+template <bool GROUP_K, int BN, int STAGES, int EPI, int LAYOUT>
 void launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, int grid, cudaStream_t stream) {
   constexpr size_t smem = 1024 + STAGES * Smem<BN>::kStageBytes + (2 * STAGES + 5) * 8 + 16;
-  auto kfn = grouped_gemm_kernel<GROUP_K, BN, STAGES, EPI>;
+  auto kfn = grouped_gemm_kernel<GROUP_K, BN, STAGES, EPI, LAYOUT>;
   static bool set = false;
   if (!set) {
     AT_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
@@ -419,25 +479,31 @@ void launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, int gri
 
 // C[rows, N] = A[rows, K] @ B[g]^T per expert segment (offsets on rows, multiples of 128).
 // epilogue: 0 = bf16 C, 1 = fp32 C, 2 = SwiGLU (H = silu(gate) * up, C = pre-activation or none)
+// b_kn: B is [G, K, N] (N contiguous, e.g. the forward weight read as its transpose)
+// instead of [G, N, K].
 void grouped_gemm_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, const OptTensor& C,
-                    const OptTensor& Hout, int64_t epilogue, at::Tensor error, int64_t num_sms, double timeout_s) {
+                    const OptTensor& Hout, int64_t epilogue, at::Tensor error, int64_t num_sms, double timeout_s,
+                    bool b_kn) {
   using namespace gemm;
   const c10::cuda::CUDAGuard guard(A.device());
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "A, B must be bf16");
-  TORCH_CHECK(A.dim() == 2 && A.stride(1) == 1 && B.dim() == 3 && B.is_contiguous(), "A [rows, K], B [G, N, K]");
+  TORCH_CHECK(A.dim() == 2 && A.stride(1) == 1 && B.dim() == 3 && B.is_contiguous(),
+              "A [rows, K], B [G, N, K] (or [G, K, N] with b_kn)");
   TORCH_CHECK(offsets.scalar_type() == at::kLong && offsets.numel() == B.size(0) + 1 && B.size(0) <= 1024,
               "offsets must be [G + 1] int64, G <= 1024");
   Args a{};
   a.G = static_cast<int>(B.size(0));
-  a.N = static_cast<int>(B.size(1));
-  a.K = static_cast<int>(B.size(2));
+  a.N = static_cast<int>(b_kn ? B.size(2) : B.size(1));
+  a.K = static_cast<int>(b_kn ? B.size(1) : B.size(2));
   a.M = static_cast<int>(A.size(0));
   TORCH_CHECK(A.size(1) == a.K && a.K % 8 == 0, "K mismatch / K % 8");
+  TORCH_CHECK(!b_kn || a.N % 64 == 0, "an MN-major B needs N % 64 == 0");
   a.offsets = offsets.data_ptr<int64_t>();
   a.error = reinterpret_cast<uint32_t*>(error.data_ptr<int32_t>());
   a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
   const CUtensorMap ma = make_map(A.data_ptr(), A.size(0), a.K, A.stride(0), BM);
-  const CUtensorMap mb = make_map(B.data_ptr(), int64_t(a.G) * a.N, a.K, a.K, 256);
+  const CUtensorMap mb = b_kn ? make_map_kn(B.data_ptr(), a.G, a.K, a.N)
+                              : make_map(B.data_ptr(), int64_t(a.G) * a.N, a.K, a.K, 256);
   a.c_rows = A.size(0);
   if (epilogue == kEpiSwiGLU) {
     TORCH_CHECK(a.N % 256 == 0 && Hout.has_value(), "SwiGLU needs N % 256 == 0 and an H output");
@@ -456,23 +522,33 @@ void grouped_gemm_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
   }
   const int sms = num_sms > 0 ? static_cast<int>(num_sms) : at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (epilogue == kEpiBF16) launch<false, 256, 4, kEpiBF16>(ma, mb, a, sms, stream);
-  else if (epilogue == kEpiF32) launch<false, 256, 4, kEpiF32>(ma, mb, a, sms, stream);
-  else launch<false, 256, 4, kEpiSwiGLU>(ma, mb, a, sms, stream);
+  if (b_kn) {
+    if (epilogue == kEpiBF16) launch<false, 256, 4, kEpiBF16, 2>(ma, mb, a, sms, stream);
+    else if (epilogue == kEpiF32) launch<false, 256, 4, kEpiF32, 2>(ma, mb, a, sms, stream);
+    else launch<false, 256, 4, kEpiSwiGLU, 2>(ma, mb, a, sms, stream);
+  } else {
+    if (epilogue == kEpiBF16) launch<false, 256, 4, kEpiBF16, 0>(ma, mb, a, sms, stream);
+    else if (epilogue == kEpiF32) launch<false, 256, 4, kEpiF32, 0>(ma, mb, a, sms, stream);
+    else launch<false, 256, 4, kEpiSwiGLU, 0>(ma, mb, a, sms, stream);
+  }
 }
 
-// C[g] (M x N) = A[:, seg_g] @ B[:, seg_g]^T with A [M, tokens], B [N, tokens] (offsets on tokens).
+// C[g] (M x N) = A[:, seg_g] @ B[:, seg_g]^T with A [M, tokens], B [N, tokens] (offsets on tokens),
+// or, with tok_major, A [tokens, M] and B [tokens, N] (the activations as they are).
 void grouped_gemm_k(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, at::Tensor C,
-                    at::Tensor error, int64_t num_sms, double timeout_s) {
+                    at::Tensor error, int64_t num_sms, double timeout_s, bool tok_major) {
   using namespace gemm;
   const c10::cuda::CUDAGuard guard(A.device());
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "A, B must be bf16");
-  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1, "A [M, tokens], B [N, tokens]");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1,
+              "A [M, tokens], B [N, tokens] (or [tokens, M], [tokens, N] with tok_major)");
   TORCH_CHECK(C.dim() == 3 && C.is_contiguous(), "C must be [G, M, N]");
   Args a{};
   a.G = static_cast<int>(C.size(0));
-  a.M = static_cast<int>(A.size(0));
-  a.N = static_cast<int>(B.size(0));
+  a.M = static_cast<int>(tok_major ? A.size(1) : A.size(0));
+  a.N = static_cast<int>(tok_major ? B.size(1) : B.size(0));
+  TORCH_CHECK(!tok_major || (a.M % 64 == 0 && a.N % 64 == 0 && A.size(0) == B.size(0)),
+              "token-major operands need M, N multiples of 64 and the same token count");
   TORCH_CHECK(C.size(1) == a.M && C.size(2) == a.N && offsets.numel() == a.G + 1 && a.G <= 1024, "shape mismatch");
   a.offsets = offsets.data_ptr<int64_t>();
   a.C = C.data_ptr();
@@ -480,12 +556,20 @@ void grouped_gemm_k(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
   a.c_group_stride = int64_t(a.M) * a.N;
   a.error = reinterpret_cast<uint32_t*>(error.data_ptr<int32_t>());
   a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
-  const CUtensorMap ma = make_map(A.data_ptr(), a.M, A.size(1), A.stride(0), BM);
-  const CUtensorMap mb = make_map(B.data_ptr(), a.N, B.size(1), B.stride(0), 256);
+  // token-major: boxes of 64 (M or N) x BK tokens, one per 64-wide MN atom
+  const CUtensorMap ma = tok_major ? make_map(A.data_ptr(), A.size(0), a.M, A.stride(0), BK)
+                                   : make_map(A.data_ptr(), a.M, A.size(1), A.stride(0), BM);
+  const CUtensorMap mb = tok_major ? make_map(B.data_ptr(), B.size(0), a.N, B.stride(0), BK)
+                                   : make_map(B.data_ptr(), a.N, B.size(1), B.stride(0), 256);
   const int sms = num_sms > 0 ? static_cast<int>(num_sms) : at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
   auto stream = at::cuda::getCurrentCUDAStream();
-  if (C.scalar_type() == at::kFloat) launch<true, 256, 4, kEpiF32>(ma, mb, a, sms, stream);
-  else launch<true, 256, 4, kEpiBF16>(ma, mb, a, sms, stream);
+  if (tok_major) {
+    if (C.scalar_type() == at::kFloat) launch<true, 256, 4, kEpiF32, 3>(ma, mb, a, sms, stream);
+    else launch<true, 256, 4, kEpiBF16, 3>(ma, mb, a, sms, stream);
+  } else {
+    if (C.scalar_type() == at::kFloat) launch<true, 256, 4, kEpiF32, 0>(ma, mb, a, sms, stream);
+    else launch<true, 256, 4, kEpiBF16, 0>(ma, mb, a, sms, stream);
+  }
 }
 
 }  // namespace b200ep

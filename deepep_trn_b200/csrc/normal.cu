@@ -431,6 +431,10 @@ __global__ void __launch_bounds__(kPullThreads) nd_pull_kernel(NdPullArgs a) {
           if (!mbar_wait(&bars[st], (phase_bits >> st) & 1u, hv.timeout_ns)) {
             report_error(hv.status, kTimeoutReady, 2, me, s_src[m], 0, 0, 1);
             tma_ok = false;
+            // let the loads still in flight (at most one per stage) land before the CTA exits
+            const int last = min(n - 1, m >= 1 ? m - 2 + a.nstages : pro - 1);
+            for (int q = m + 1; q <= last; ++q)
+              mbar_wait(&bars[q % a.nstages], (phase_bits >> (q % a.nstages)) & 1u, hv.timeout_ns);
             break;
           }
           phase_bits ^= 1u << st;
@@ -958,15 +962,17 @@ __global__ void __launch_bounds__(kCombThreads) nc_pull_kernel(NcPullArgs a) {
     int tok = 0;
     for (int k = 0; k < nrows; ++k, ++g) {
       const int st = static_cast<int>(g % a.nstages);
-      if (!mbar_wait(&bars[st], (g / a.nstages) & 1u, hv.timeout_ns)) {
-        if (tid == 0) report_error(hv.status, kTimeoutCombine, 3, me, -1, 0, 0, 2);
-        return;
-      }
-      const uint8_t* row = smem_ring + static_cast<int64_t>(st) * a.stage_bytes;
+      // a timed-out thread skips the row and raises s_fail; every thread still reaches the
+      // barrier below, and the whole CTA stops after it
+      if (mbar_wait(&bars[st], (g / a.nstages) & 1u, hv.timeout_ns)) {
+        const uint8_t* row = smem_ring + static_cast<int64_t>(st) * a.stage_bytes;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = tid + u * kCombThreads;
-        if (j < nch) acc8<T16>(acc[u], *reinterpret_cast<const int4*>(row + j * 16));
+        for (int u = 0; u < 4; ++u) {
+          const int j = tid + u * kCombThreads;
+          if (j < nch) acc8<T16>(acc[u], *reinterpret_cast<const int4*>(row + j * 16));
+        }
+      } else {
+        s_fail = 1;
       }
       while (s_n[tok + 1] <= k) ++tok;
       if (k + 1 == s_n[tok + 1]) {
@@ -989,6 +995,15 @@ __global__ void __launch_bounds__(kCombThreads) nc_pull_kernel(NcPullArgs a) {
         }
       }
       __syncthreads();  // every thread is done with stage st
+      if (s_fail) {
+        if (tid == 0) {
+          report_error(hv.status, kTimeoutCombine, 3, me, -1, 0, 0, 2);
+          // let the loads still in flight land before the CTA's shared memory is released
+          for (int kk = k + 1; kk < nrows && kk < k + a.nstages; ++kk)
+            mbar_wait(&bars[(g + kk - k) % a.nstages], ((g + kk - k) / a.nstages) & 1u, hv.timeout_ns);
+        }
+        return;
+      }
       if (tid == 0 && k + a.nstages < nrows) issue(k + a.nstages, g + a.nstages);
     }
     // tokens routed nowhere (all top-k masked) still get bias (or zeros)

@@ -85,9 +85,10 @@ void fence_cost(SymmHeap& heap, int64_t peer, int64_t bytes, int64_t scope, at::
 
 // gemm.cu
 void grouped_gemm_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, const OptTensor& C,
-                    const OptTensor& Hout, int64_t epilogue, at::Tensor error, int64_t num_sms, double timeout_s);
+                    const OptTensor& Hout, int64_t epilogue, at::Tensor error, int64_t num_sms, double timeout_s,
+                    bool b_kn);
 void grouped_gemm_k(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, at::Tensor C,
-                    at::Tensor error, int64_t num_sms, double timeout_s);
+                    at::Tensor error, int64_t num_sms, double timeout_s, bool tok_major);
 
 // moe.cu
 void router_topk(const at::Tensor& logits, int64_t topk, at::Tensor idx, at::Tensor w);

@@ -25,6 +25,7 @@ import torch.nn as nn
 
 from ..ops import gemm as G
 from ..ops import moe_ops as MO
+from ..utils.profiling import timer
 
 
 _OFFS: dict = {}
@@ -54,18 +55,24 @@ class _MoEFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, Wr, W1, W2, buf, num_experts, topk, router_bias=None):
         EL = num_experts // buf.group_size
-        logits = router_logits(x, Wr)
-        if router_bias is not None:
-            logits = logits + router_bias
-        idx, w = MO.router_topk(logits, topk)
-        ntr, _, nte, itr, _ = buf.get_dispatch_layout(idx, num_experts)
-        recv_x, recv_idx, recv_w, per_expert, handle, _ = buf.dispatch(
-            x, topk_idx=idx, topk_weights=w, num_tokens_per_rank=ntr, is_token_in_rank=itr,
-            num_tokens_per_expert=nte)
-        rows, pos, offsets, counts = MO.permute(recv_x, recv_idx, EL, per_expert)
-        h, pre, o = _expert_forward(rows, offsets, W1, W2)
-        y_recv = MO.unpermute(o, pos, recv_w)
-        y, _, _ = buf.combine(y_recv, handle)
+        with timer.stage('moe.router'):
+            logits = router_logits(x, Wr)
+            if router_bias is not None:
+                logits = logits + router_bias
+            idx, w = MO.router_topk(logits, topk)
+        with timer.stage('moe.dispatch'):
+            ntr, _, nte, itr, _ = buf.get_dispatch_layout(idx, num_experts)
+            recv_x, recv_idx, recv_w, per_expert, handle, _ = buf.dispatch(
+                x, topk_idx=idx, topk_weights=w, num_tokens_per_rank=ntr, is_token_in_rank=itr,
+                num_tokens_per_expert=nte)
+        with timer.stage('moe.permute'):
+            rows, pos, offsets, counts = MO.permute(recv_x, recv_idx, EL, per_expert)
+        with timer.stage('moe.experts'):
+            h, pre, o = _expert_forward(rows, offsets, W1, W2)
+        with timer.stage('moe.unpermute'):
+            y_recv = MO.unpermute(o, pos, recv_w)
+        with timer.stage('moe.combine'):
+            y, _, _ = buf.combine(y_recv, handle)
         ctx.save_for_backward(x, Wr, W1, W2, idx, w, recv_w, pos, offsets, counts, rows, pre, h, o)
         ctx.buf, ctx.handle, ctx.num_experts = buf, handle, num_experts
         return y
@@ -75,21 +82,34 @@ class _MoEFunction(torch.autograd.Function):
         x, Wr, W1, W2, idx, w, recv_w, pos, offsets, counts, rows, pre, h, o = ctx.saved_tensors
         buf, handle = ctx.buf, ctx.handle
         dy = dy.contiguous().to(x.dtype)
-        dy_recv, *_ = buf.dispatch(dy, handle=handle)                 # combine backward
-        d_o, d_recv_w = MO.unpermute_bwd(dy_recv, o, pos, recv_w, offsets, counts)
-        dh = G.grouped_gemm(d_o, MO.transpose(W2), offsets)            # [P, I]
-        dpre = MO.swiglu_bwd(dh, pre)                                  # [P, 2I]
-        drows = G.grouped_gemm(dpre, MO.transpose(W1), offsets)        # [P, H]
-        dW2 = G.grouped_gemm_wgrad(MO.transpose(d_o), MO.transpose(h), offsets, out_dtype=torch.float32)
-        dW1 = G.grouped_gemm_wgrad(MO.transpose(dpre), MO.transpose(rows), offsets, out_dtype=torch.float32)
-        d_recv_x = MO.permute_bwd(drows, pos)
-        dx, dw, _ = buf.combine(d_recv_x, handle, topk_weights=d_recv_w)   # dispatch backward
-        dlogits = MO.router_topk_bwd(idx, w, dw.float(), ctx.num_experts).to(x.dtype)
-        seg = _single_segment(x.shape[0], x.device)
-        dx_router = G.grouped_gemm(dlogits, MO.transpose(Wr).unsqueeze(0), seg, epilogue='f32')   # [T, H]
-        dx = (dx.float() + dx_router).to(x.dtype)
-        dWr = G.grouped_gemm_wgrad(MO.transpose(dlogits), MO.transpose(x), seg)[0]               # [E, H]
-        return dx, dWr.to(Wr.dtype), dW1.to(W1.dtype), dW2.to(W2.dtype), None, None, None, None
+        with timer.stage('moe.bwd.dispatch'):
+            dy_recv, *_ = buf.dispatch(dy, handle=handle)                 # combine backward
+        with timer.stage('moe.bwd.unpermute'):
+            d_o, d_recv_w = MO.unpermute_bwd(dy_recv, o, pos, recv_w, offsets, counts)
+        # transposed operands are read in place by the GEMM (MN-major tiles); fp32 accumulation,
+        # one rounding to the weight dtype
+        with timer.stage('moe.bwd.dgrad'):
+            dh = G.grouped_gemm(d_o, W2, offsets, b_layout='kn')           # [P, I] = d_o @ W2[e]
+            dpre = MO.swiglu_bwd(dh, pre)                                  # [P, 2I]
+            drows = G.grouped_gemm(dpre, W1, offsets, b_layout='kn')       # [P, H] = dpre @ W1[e]
+        with timer.stage('moe.bwd.wgrad'):
+            dW2 = G.grouped_gemm_wgrad(d_o, h, offsets, out_dtype=W2.dtype)      # [EL, H, I]
+            dW1 = G.grouped_gemm_wgrad(dpre, rows, offsets, out_dtype=W1.dtype)  # [EL, 2I, H]
+        with timer.stage('moe.bwd.permute'):
+            d_recv_x = MO.permute_bwd(drows, pos)
+        with timer.stage('moe.bwd.combine'):
+            dx, dw, _ = buf.combine(d_recv_x, handle, topk_weights=d_recv_w)   # dispatch backward
+        with timer.stage('moe.bwd.router'):
+            dlogits = MO.router_topk_bwd(idx, w, dw.float(), ctx.num_experts).to(x.dtype)
+            seg = _single_segment(x.shape[0], x.device)
+            dx_router = G.grouped_gemm(dlogits, Wr.unsqueeze(0), seg, epilogue='f32', b_layout='kn')  # [T, H]
+            dx = (dx.float() + dx_router).to(x.dtype)
+            if ctx.num_experts % 64 == 0:
+                dWr = G.grouped_gemm_wgrad(dlogits, x, seg, out_dtype=Wr.dtype)[0]            # [E, H]
+            else:  # the token-major operand path tiles M in 64-wide atoms
+                dWr = G.grouped_gemm_wgrad(MO.transpose(dlogits), MO.transpose(x), seg, out_dtype=Wr.dtype,
+                                           layout='mk')[0]
+        return dx, dWr, dW1, dW2, None, None, None, None
 
 
 class MoELayer(nn.Module):

@@ -1,7 +1,12 @@
 """Grouped expert GEMMs on tcgen05 tensor cores (N7) with fused SwiGLU (N8).
 
-``grouped_gemm``       C[seg_e] = A[seg_e] @ B[e]^T      A [rows, K], B [G, N, K]   (forward, dX)
-``grouped_gemm_wgrad`` C[e] = A[:, seg_e] @ B[:, seg_e]^T A [M, tok], B [N, tok]    (dW)
+``grouped_gemm``       C[seg_e] = A[seg_e] @ B[e]^T      A [rows, K], B [G, N, K]   (forward)
+                       C[seg_e] = A[seg_e] @ B[e]        A [rows, K], B [G, K, N]   (``b_layout='kn'``: dX)
+``grouped_gemm_wgrad`` C[e] = A[seg_e]^T @ B[seg_e]      A [tok, M], B [tok, N]     (dW)
+                       C[e] = A[:, seg_e] @ B[:, seg_e]^T A [M, tok], B [N, tok]    (``layout='mk'``)
+
+Transposed operands are read in place by the tensor cores (MN-major shared-memory
+descriptors), never materialised.
 
 Segments are given by ``offsets`` [G + 1] int64 on the device, multiples of 128
 (``permute`` pads every expert's rows to that). The kernels read the offsets on
@@ -35,26 +40,33 @@ def check(device=None) -> None:
 
 def grouped_gemm(A: torch.Tensor, B: torch.Tensor, offsets: torch.Tensor, out: torch.Tensor | None = None,
                  epilogue: str = 'bf16', h_out: torch.Tensor | None = None, save_preact: bool = True,
-                 num_sms: int = 0, timeout_s: float = 10.0):
-    """Returns C (or ``(h, pre_activation)`` for ``epilogue='swiglu'``)."""
-    rows, N = A.shape[0], B.shape[1]
+                 num_sms: int = 0, timeout_s: float = 10.0, b_layout: str = 'nk'):
+    """Returns C (or ``(h, pre_activation)`` for ``epilogue='swiglu'``). ``b_layout='kn'``
+    takes B as [G, K, N] (e.g. a forward weight, for the input gradient)."""
+    kn = b_layout == 'kn'
+    rows, N = A.shape[0], B.shape[2 if kn else 1]
     if epilogue == 'swiglu':
         h = h_out if h_out is not None else torch.empty(rows, N // 2, dtype=torch.bfloat16, device=A.device)
         c = (out if out is not None else torch.empty(rows, N, dtype=torch.bfloat16, device=A.device)) \
             if save_preact else None
-        load().grouped_gemm_m(A, B, offsets, c, h, 2, _err(A.device), num_sms, timeout_s)
+        load().grouped_gemm_m(A, B, offsets, c, h, 2, _err(A.device), num_sms, timeout_s, kn)
         return h, c
     dtype = torch.float32 if epilogue == 'f32' else torch.bfloat16
     c = out if out is not None else torch.empty(rows, N, dtype=dtype, device=A.device)
-    load().grouped_gemm_m(A, B, offsets, c, None, EPILOGUES[epilogue], _err(A.device), num_sms, timeout_s)
+    load().grouped_gemm_m(A, B, offsets, c, None, EPILOGUES[epilogue], _err(A.device), num_sms, timeout_s, kn)
     return c
 
 
 def grouped_gemm_wgrad(A: torch.Tensor, B: torch.Tensor, offsets: torch.Tensor, out_dtype=torch.float32,
-                       out: torch.Tensor | None = None, num_sms: int = 0, timeout_s: float = 10.0):
+                       out: torch.Tensor | None = None, num_sms: int = 0, timeout_s: float = 10.0,
+                       layout: str = 'tok'):
+    """Per-expert A_e^T B_e over each token segment: ``[G, M, N]``. ``layout='tok'`` takes the
+    activations as they are (A [tok, M], B [tok, N]); ``'mk'`` takes them transposed."""
     G = offsets.numel() - 1
-    c = out if out is not None else torch.empty(G, A.shape[0], B.shape[0], dtype=out_dtype, device=A.device)
-    load().grouped_gemm_k(A, B, offsets, c, _err(A.device), num_sms, timeout_s)
+    tok = layout == 'tok'
+    M, N = (A.shape[1], B.shape[1]) if tok else (A.shape[0], B.shape[0])
+    c = out if out is not None else torch.empty(G, M, N, dtype=out_dtype, device=A.device)
+    load().grouped_gemm_k(A, B, offsets, c, _err(A.device), num_sms, timeout_s, tok)
     return c
 
 

@@ -219,7 +219,14 @@ class NvlinkEngine:
             recv_counts = handle.recv_counts if cached else None
         else:
             with timer.stage('notify_wait'):
-                info = self.heap.wait_notify(self.ticket, EL, self.host_timeout_s)
+                try:
+                    info = self.heap.wait_notify(self.ticket, EL, self.host_timeout_s)
+                except RuntimeError:
+                    # every wait of the queued kernels is bounded: let them finish so nothing of
+                    # this op is in flight, then raise with the device's own record
+                    torch.cuda.synchronize()
+                    self.check()
+                    raise
             N = int(info[0])
             recv_counts = torch.tensor(info[1:1 + self.R], dtype=torch.int64)
             per_expert = info[1 + self.R:1 + self.R + EL]

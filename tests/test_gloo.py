@@ -73,3 +73,20 @@ REF = __import__('pathlib').Path(__file__).resolve().parents[1] / 'baseline' / '
 def test_reference_parity_gloo(run_dist, nproc):
     rc, out = run_dist('ref_parity.py', nproc, timeout=600)
     assert rc == 0 and 'REF_PARITY_PASS' in out, out[-4000:]
+
+
+@pytest.mark.parametrize('case', ['config', 'exit', 'counts'])
+def test_host_made_failures_raise(run_dist, case):
+    """Failures made on the host end in exceptions on the ranks that can see them, not in hangs."""
+    import re
+    rc, out = run_dist('failures.py', 3, '--case', case, timeout=240, env={'B200EP_PG_TIMEOUT': '20'})
+    lines = re.findall(r'RANK=(\d+) (DETECTED=\w+|UNDETECTED)', out)
+    status = {int(r): s for r, s in lines}
+    if case == 'config':
+        assert rc == 0 and all(status.get(r) == 'DETECTED=ValueError' for r in range(3)), out[-3000:]
+    elif case == 'exit':
+        assert 'RANK=2 LEAVING' in out, out[-3000:]
+        assert all(status.get(r, '').startswith('DETECTED=') for r in (0, 1)), out[-3000:]
+    else:
+        assert rc == 0 and len(status) == 3, out[-3000:]
+        assert any(s == 'DETECTED=RuntimeError' for s in status.values()), out[-3000:]

@@ -126,3 +126,12 @@ def test_smoke_entry():
     p = subprocess.run([sys.executable, os.path.join(root, '__graft_entry__.py')], capture_output=True, text=True,
                        timeout=600, cwd=root)
     assert p.returncode == 0 and 'smoke OK' in p.stdout, p.stdout + p.stderr
+
+
+@needs_cuda
+@pytest.mark.skipif(_ngpus() < 2, reason='needs 2 GPUs')
+@pytest.mark.parametrize('case', ['normal', 'll'])
+def test_absent_peer_times_out_cleanly(run_dist, case):
+    # rank 1 skips the op; rank 0's bounded waits must turn into a DeviceError within seconds
+    rc, out = run_dist('peer_absent.py', 2, '--case', case, timeout=300, env={'NCCL_NVLS_ENABLE': '0'})
+    assert rc == 0 and 'PEER_ABSENT_PASS' in out, out[-6000:]

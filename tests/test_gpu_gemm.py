@@ -82,10 +82,36 @@ def test_grouped_gemm_wgrad():
     for e in range(G):  # padding columns are zero, as permute leaves them
         At[:, offs[e] + counts[e]:offs[e + 1]] = 0
         Bt[:, offs[e] + counts[e]:offs[e + 1]] = 0
-    C = grouped_gemm_wgrad(At, Bt, torch.tensor(offs, device='cuda'))
+    o = torch.tensor(offs, device='cuda')
+    C = grouped_gemm_wgrad(At, Bt, o, layout='mk')
+    # the same product from the untransposed activations (MN-major operands), bf16 out
+    Ct = grouped_gemm_wgrad(At.t().contiguous(), Bt.t().contiguous(), o, out_dtype=torch.bfloat16)
     torch.cuda.synchronize()
     check()
     for e in range(G):
         s, t = offs[e], offs[e + 1]
         ref = At[:, s:t].float() @ Bt[:, s:t].float().t()
         _close(C[e], ref, tol=1e-3)
+        _close(Ct[e], ref, tol=1e-2)
+
+
+@needs_cuda
+@pytest.mark.parametrize('G,counts,N,K', [
+    (3, [128, 0, 256], 256, 256),
+    (2, [100, 300], 192, 200),       # N tail inside a 256 tile, K tail inside a 64 block
+    (4, [1024, 896, 128, 1280], 7168, 2048),
+])
+def test_grouped_gemm_b_kn(G, counts, N, K):
+    # B given as [G, K, N] (the forward weight for the input gradient), read MN-major in place
+    from deepep_trn_b200.ops.gemm import check, grouped_gemm
+    torch.manual_seed(3)
+    offs = _segments(counts)
+    A = (torch.randn(offs[-1], K, device='cuda') * 0.5).to(torch.bfloat16)
+    B = (torch.randn(G, K, N, device='cuda') * 0.05).to(torch.bfloat16)
+    o = torch.tensor(offs, dtype=torch.int64, device='cuda')
+    C = grouped_gemm(A, B, o, b_layout='kn')
+    torch.cuda.synchronize()
+    check()
+    for e in range(G):
+        s, t = offs[e], offs[e] + counts[e]
+        _close(C[s:t], A[s:t].float() @ B[e].float())
