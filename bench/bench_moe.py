@@ -32,6 +32,7 @@ def main():
     p.add_argument('--experts', type=int, default=256)
     p.add_argument('--topk', type=int, default=8)
     p.add_argument('--steps', type=int, default=5)
+    p.add_argument('--warmup', type=int, default=3)
     p.add_argument('--impls', default='ours,nccl')
     p.add_argument('--breakdown', action='store_true', help='per-phase device time of the fused layer')
     p.set_defaults(tokens=[4096])
@@ -76,7 +77,7 @@ def main():
             y.backward(dy)
             return y
 
-        for _ in range(2):
+        for _ in range(args.warmup):
             step()
         torch.cuda.synchronize()
         dist.barrier(group=ctx.control)
@@ -84,9 +85,10 @@ def main():
         for _ in range(args.steps):
             timer.run(step)
         ms = max_over_ranks(timer.total_ms()) / args.steps
+        per_step = [round(st.elapsed_time(en), 3) for st, en in timer.events]
         flops = 18.0 * T * K * H * I  # expert GEMMs per rank on average: forward 6*P*H*I, backward twice that
         results[impl] = dict(ms_per_step=round(ms, 3), tokens_per_s=round(T * ctx.ep / (ms * 1e-3), 1),
-                             expert_tflops_per_rank=round(flops / (ms * 1e-3) / 1e12, 1))
+                             expert_tflops_per_rank=round(flops / (ms * 1e-3) / 1e12, 1), steps_ms_rank0=per_step)
         if args.breakdown and impl == 'ours':
             from deepep_trn_b200.utils.profiling import timer
             timer.reset()

@@ -20,7 +20,10 @@
 //               back to the producer and each finished tile to the epilogue.
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (thread = row), fused
 //               activation (SwiGLU on interleaved gate/up blocks) and the bf16/fp32
-//               cast, stores to global, then frees the accumulator.
+//               cast into a swizzled 32x32 box in shared memory, which one lane
+//               stores with a TMA tensor store (the map clips rows and columns past
+//               the output's extent); the accumulator is freed as soon as it has
+//               been read, so the stores overlap the next tile's MMAs.
 // Every mbarrier wait is bounded; on timeout the CTA records an error, stops
 // issuing, frees its TMEM and returns.
 #include <ATen/cuda/CUDAContext.h>
@@ -69,6 +72,17 @@ __device__ __forceinline__ void tma_load_3d(void* smem, const CUtensorMap* map, 
       "[%2];" ::"r"(smem_u32(smem)),
       "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
+}
+// shared -> global tensor stores (bulk async-group of the calling thread)
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(smem)), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
+               "r"(smem_u32(smem)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
@@ -164,6 +178,28 @@ struct Smem {
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
 };
+// Epilogue staging: per epilogue warp, a ring of 32 x 32 output boxes (2 KB bf16 with
+// 64-byte rows and SWIZZLE_64B, or 4 KB fp32 with 128-byte rows and SWIZZLE_128B).
+constexpr int kEpiWarpBytes = 4096;
+constexpr int kEpiBytes = 4 * kEpiWarpBytes;
+
+// Row r (= lane) of a 32 x 32 box into its swizzled slot: 16-byte chunk c of the row
+// goes to chunk c ^ (swizzle phase of row r), the pattern the tensor map's swizzle mode
+// undoes on the way out; the 8 rows of each 128-byte bank window land in distinct banks.
+__device__ __forceinline__ void put_row_bf16(uint8_t* slot, int r, const uint32_t (&v)[16]) {
+  const int4* src = reinterpret_cast<const int4*>(v);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) *reinterpret_cast<int4*>(slot + r * 64 + ((c ^ ((r >> 1) & 3)) << 4)) = src[c];
+}
+__device__ __forceinline__ void put_row_f32(uint8_t* slot, int r, const uint32_t (&v)[32]) {
+  const int4* src = reinterpret_cast<const int4*>(v);
+#pragma unroll
+  for (int c = 0; c < 8; ++c) *reinterpret_cast<int4*>(slot + r * 128 + ((c ^ (r & 7)) << 4)) = src[c];
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&p);
+}
 
 // Tile t -> (group, m0 / k range, n0). Returns false past the end.
 struct Tile {
@@ -209,14 +245,16 @@ __device__ __forceinline__ bool tile_of(int t, const Args& a, const int64_t* off
 // through a 3-D map so a K tail never reaches into the next expert's weight).
 template <bool GROUP_K, int BN, int STAGES, int EPI, int LAYOUT>
 __global__ void __launch_bounds__(kThreads, 1)
-    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args a) {
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmH, Args a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   using S = Smem<BN>;
   constexpr bool A_MN = (LAYOUT & 1) != 0, B_MN = (LAYOUT & 2) != 0;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * S::kBBytes);
+  uint8_t* sE = sB + STAGES * S::kBBytes;  // epilogue staging, kEpiWarpBytes per epilogue warp
+  uint64_t* full = reinterpret_cast<uint64_t*>(sE + kEpiBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -241,6 +279,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    prefetch_tmap(&tmC);
+    if (EPI == kEpiSwiGLU) prefetch_tmap(&tmH);
   }
   if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
@@ -319,7 +359,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int q = warp & 3;                    // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;             // accumulator row of this thread
+    uint8_t* ring = sE + (warp - 2) * kEpiWarpBytes;
+    constexpr int kSlot = EPI == kEpiF32 ? 4096 : 2048;
+    constexpr int kSlots = kEpiWarpBytes / kSlot;
+    uint32_t nst = 0;                          // boxes this warp has stored (ring position)
+    // one 32 x 32 box: wait until its slot's previous store has read it, fill, store
+    auto store_box = [&](const CUtensorMap* map, auto&& fill, int x, int y, int g) {
+      uint8_t* slot = ring + (nst % kSlots) * kSlot;
+      if (lane == 0) bulk_wait_read<kSlots - 1>();
+      __syncwarp();
+      fill(slot);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (GROUP_K) tma_store_3d(map, slot, x, y, g);
+        else tma_store_2d(map, slot, x, y);
+        bulk_commit();
+      }
+      ++nst;
+    };
     uint32_t acc = 0;
     Tile tl;
     for (int t = blockIdx.x; tile_of<GROUP_K, BN>(t, a, s_offs, tl); t += gridDim.x) {
@@ -331,39 +389,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
       }
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * 256;
-      const int64_t grow = static_cast<int64_t>(tl.m0) + row;
+      const int row0 = tl.m0 + q * 32;         // first row of this warp's boxes
+      // boxes that start past the output are skipped; the map clips partial ones
+      const bool rows_in = GROUP_K ? row0 < a.M : row0 < a.c_rows;
       if (EPI == kEpiSwiGLU) {
         // tile = [128 gate columns | 128 up columns] of the interleaved weight layout
-        __nv_bfloat16* hrow = static_cast<__nv_bfloat16*>(a.H) + grow * a.ldh + tl.n0 / 2;
-        __nv_bfloat16* crow = a.C ? static_cast<__nv_bfloat16*>(a.C) + grow * a.ldc + tl.n0 : nullptr;
-        const bool srow = grow < a.c_rows;
 #pragma unroll 1
         for (int c = 0; c < BN / 2; c += 32) {
           uint32_t g[32], u[32];
           tmem_ld32(taddr + c, g);
           tmem_ld32(taddr + BN / 2 + c, u);
-          alignas(16) __nv_bfloat16 hv[32], gv[32], uv[32];
+          if (!rows_in) continue;
+          uint32_t hv[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float gf = __uint_as_float(g[i]), uf = __uint_as_float(u[i]);
-            hv[i] = __float2bfloat16_rn(silu(gf) * uf);
-            gv[i] = __float2bfloat16_rn(gf);
-            uv[i] = __float2bfloat16_rn(uf);
+          for (int i = 0; i < 16; ++i) {
+            const float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
+            const float u0 = __uint_as_float(u[2 * i]), u1 = __uint_as_float(u[2 * i + 1]);
+            hv[i] = pack_bf16(silu(g0) * u0, silu(g1) * u1);
           }
-          if (!srow) continue;
+          store_box(&tmH, [&](uint8_t* sl) { put_row_bf16(sl, lane, hv); }, tl.n0 / 2 + c, row0, 0);
+          if (a.C) {
+            uint32_t pv[16];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) reinterpret_cast<int4*>(hrow + c)[i] = reinterpret_cast<int4*>(hv)[i];
-          if (crow) {
+            for (int i = 0; i < 16; ++i) pv[i] = pack_bf16(__uint_as_float(g[2 * i]), __uint_as_float(g[2 * i + 1]));
+            store_box(&tmC, [&](uint8_t* sl) { put_row_bf16(sl, lane, pv); }, tl.n0 + c, row0, 0);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              reinterpret_cast<int4*>(crow + c)[i] = reinterpret_cast<int4*>(gv)[i];
-              reinterpret_cast<int4*>(crow + BN / 2 + c)[i] = reinterpret_cast<int4*>(uv)[i];
-            }
+            for (int i = 0; i < 16; ++i) pv[i] = pack_bf16(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
+            store_box(&tmC, [&](uint8_t* sl) { put_row_bf16(sl, lane, pv); }, tl.n0 + BN / 2 + c, row0, 0);
           }
         }
       } else {
-        const int64_t cbase = GROUP_K ? static_cast<int64_t>(tl.g) * a.c_group_stride : 0;
-        const bool rok = GROUP_K ? (tl.m0 + row < a.M) : (grow < a.c_rows);
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
           uint32_t r[32];
@@ -373,29 +428,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) r[i] = 0u;
           }
-          const int n = tl.n0 + c;
-          if (!rok || n >= a.N) continue;
+          if (!rows_in || tl.n0 + c >= a.N) continue;
           if (EPI == kEpiF32) {
-            float* crow = static_cast<float*>(a.C) + cbase + grow * a.ldc + n;
-            if (n + 32 <= a.N) {
-#pragma unroll
-              for (int i = 0; i < 8; ++i)
-                reinterpret_cast<float4*>(crow)[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                                                 __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
-            } else {
-              for (int i = 0; i < a.N - n; ++i) crow[i] = __uint_as_float(r[i]);
-            }
+            store_box(&tmC, [&](uint8_t* sl) { put_row_f32(sl, lane, r); }, tl.n0 + c, row0, tl.g);
           } else {
-            __nv_bfloat16* crow = static_cast<__nv_bfloat16*>(a.C) + cbase + grow * a.ldc + n;
-            alignas(16) __nv_bfloat16 v[32];
+            uint32_t v[16];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __float2bfloat16_rn(__uint_as_float(r[i]));
-            if (n + 32 <= a.N) {
-#pragma unroll
-              for (int i = 0; i < 4; ++i) reinterpret_cast<int4*>(crow)[i] = reinterpret_cast<int4*>(v)[i];
-            } else {
-              for (int i = 0; i < a.N - n; ++i) crow[i] = v[i];
-            }
+            for (int i = 0; i < 16; ++i) v[i] = pack_bf16(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+            store_box(&tmC, [&](uint8_t* sl) { put_row_bf16(sl, lane, v); }, tl.n0 + c, row0, tl.g);
           }
         }
       }
@@ -405,6 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++acc;
       }
     }
+    if (lane == 0) bulk_wait<0>();  // this warp's stores are complete before the CTA exits
   }
   tc_fence_before();
   __syncthreads();
@@ -462,16 +503,40 @@ CUtensorMap make_map_kn(const void* base, int64_t G, int64_t K, int64_t N) {
   return m;
 }
 
+// Output map for the epilogue's 32 x 32 boxes. 2-D [rows, cols] (row stride ld) or, with
+// groups > 0, 3-D [groups, rows, cols] (group stride rows * ld) so a partial box never
+// writes into the next group. fp32 boxes have 128-byte rows (SWIZZLE_128B), bf16 boxes
+// 64-byte rows (SWIZZLE_64B).
+CUtensorMap make_out_map(void* base, bool f32, int64_t rows, int64_t cols, int64_t ld, int64_t groups) {
+  const int64_t es = f32 ? 4 : 2;
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "output base must be 16-byte aligned");
+  TORCH_CHECK((ld * es) % 16 == 0, "output row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  const cuuint32_t rank = groups > 0 ? 3 : 2;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(groups > 0 ? groups : 1)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * es), static_cast<cuuint64_t>(rows * ld * es)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encoder()(&m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, base,
+                         dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                         CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (output) failed: ", static_cast<int>(r));
+  return m;
+}
+
 template <bool GROUP_K, int BN, int STAGES, int EPI, int LAYOUT>
-void launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& a, int grid, cudaStream_t stream) {
-  constexpr size_t smem = 1024 + STAGES * Smem<BN>::kStageBytes + (2 * STAGES + 5) * 8 + 16;
+void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mh,
+            const Args& a, int grid, cudaStream_t stream) {
+  constexpr size_t smem = 1024 + STAGES * Smem<BN>::kStageBytes + kEpiBytes + (2 * STAGES + 5) * 8 + 16;
   auto kfn = grouped_gemm_kernel<GROUP_K, BN, STAGES, EPI, LAYOUT>;
   static bool set = false;
   if (!set) {
     AT_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
     set = true;
   }
-  kfn<<<grid, kThreads, smem, stream>>>(ma, mb, a);
+  kfn<<<grid, kThreads, smem, stream>>>(ma, mb, mc, mh, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -513,23 +578,26 @@ void grouped_gemm_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
   }
   if (C.has_value()) {
     TORCH_CHECK(C->size(0) >= A.size(0) && C->stride(1) == 1, "C needs at least as many rows as A");
-    TORCH_CHECK(epilogue != kEpiF32 || a.ldc % 4 == 0, "fp32 C rows must be 16-byte aligned");
+    TORCH_CHECK((epilogue == kEpiF32) == (C->scalar_type() == at::kFloat), "C dtype does not match the epilogue");
     a.C = C->data_ptr();
     a.ldc = C->stride(0);
-    TORCH_CHECK(a.ldc % 8 == 0 && (reinterpret_cast<uintptr_t>(a.C) & 15) == 0, "C rows must be 16-byte aligned");
   } else {
     TORCH_CHECK(epilogue == kEpiSwiGLU, "C is required");
   }
+  // output maps: rows past A's (the padding of the last segment) are clipped by the map
+  const CUtensorMap mh = epilogue == kEpiSwiGLU ? make_out_map(a.H, false, a.c_rows, a.N / 2, a.ldh, 0)
+                                                : CUtensorMap{};
+  const CUtensorMap mc = a.C ? make_out_map(a.C, epilogue == kEpiF32, a.c_rows, a.N, a.ldc, 0) : mh;
   const int sms = num_sms > 0 ? static_cast<int>(num_sms) : at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
   auto stream = at::cuda::getCurrentCUDAStream();
   if (b_kn) {
-    if (epilogue == kEpiBF16) launch<false, 256, 4, kEpiBF16, 2>(ma, mb, a, sms, stream);
-    else if (epilogue == kEpiF32) launch<false, 256, 4, kEpiF32, 2>(ma, mb, a, sms, stream);
-    else launch<false, 256, 4, kEpiSwiGLU, 2>(ma, mb, a, sms, stream);
+    if (epilogue == kEpiBF16) launch<false, 256, 4, kEpiBF16, 2>(ma, mb, mc, mh, a, sms, stream);
+    else if (epilogue == kEpiF32) launch<false, 256, 4, kEpiF32, 2>(ma, mb, mc, mh, a, sms, stream);
+    else launch<false, 256, 4, kEpiSwiGLU, 2>(ma, mb, mc, mh, a, sms, stream);
   } else {
-    if (epilogue == kEpiBF16) launch<false, 256, 4, kEpiBF16, 0>(ma, mb, a, sms, stream);
-    else if (epilogue == kEpiF32) launch<false, 256, 4, kEpiF32, 0>(ma, mb, a, sms, stream);
-    else launch<false, 256, 4, kEpiSwiGLU, 0>(ma, mb, a, sms, stream);
+    if (epilogue == kEpiBF16) launch<false, 256, 4, kEpiBF16, 0>(ma, mb, mc, mh, a, sms, stream);
+    else if (epilogue == kEpiF32) launch<false, 256, 4, kEpiF32, 0>(ma, mb, mc, mh, a, sms, stream);
+    else launch<false, 256, 4, kEpiSwiGLU, 0>(ma, mb, mc, mh, a, sms, stream);
   }
 }
 
@@ -561,14 +629,17 @@ void grouped_gemm_k(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
                                    : make_map(A.data_ptr(), a.M, A.size(1), A.stride(0), BM);
   const CUtensorMap mb = tok_major ? make_map(B.data_ptr(), B.size(0), a.N, B.stride(0), BK)
                                    : make_map(B.data_ptr(), a.N, B.size(1), B.stride(0), 256);
+  TORCH_CHECK(C.scalar_type() == at::kFloat || C.scalar_type() == at::kBFloat16, "C must be fp32 or bf16");
+  const bool f32 = C.scalar_type() == at::kFloat;
+  const CUtensorMap mc = make_out_map(a.C, f32, a.M, a.N, a.N, a.G);
   const int sms = num_sms > 0 ? static_cast<int>(num_sms) : at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
   auto stream = at::cuda::getCurrentCUDAStream();
   if (tok_major) {
-    if (C.scalar_type() == at::kFloat) launch<true, 256, 4, kEpiF32, 3>(ma, mb, a, sms, stream);
-    else launch<true, 256, 4, kEpiBF16, 3>(ma, mb, a, sms, stream);
+    if (f32) launch<true, 256, 4, kEpiF32, 3>(ma, mb, mc, mc, a, sms, stream);
+    else launch<true, 256, 4, kEpiBF16, 3>(ma, mb, mc, mc, a, sms, stream);
   } else {
-    if (C.scalar_type() == at::kFloat) launch<true, 256, 4, kEpiF32, 0>(ma, mb, a, sms, stream);
-    else launch<true, 256, 4, kEpiBF16, 0>(ma, mb, a, sms, stream);
+    if (f32) launch<true, 256, 4, kEpiF32, 0>(ma, mb, mc, mc, a, sms, stream);
+    else launch<true, 256, 4, kEpiBF16, 0>(ma, mb, mc, mc, a, sms, stream);
   }
 }
 
