@@ -146,7 +146,7 @@ def main():
     torch.cuda.synchronize()
     dist.barrier(group=control)
     timer = DeviceTimer()
-    with ClockSampler(list(range(world))) as clocks:
+    with ClockSampler(local) as clocks:
         torch.cuda.synchronize()
         dist.barrier(group=control)
         for _ in range(args.steps):
@@ -205,7 +205,9 @@ def main():
     if not args.no_ll and args.impl == 'ours':
         ll = bench_ll(args, buf, rank, dev, control)
 
-    clk = clocks.summary()
+    summaries = [None] * world
+    dist.all_gather_object(summaries, clocks.summary(), group=control)
+    clk = ClockSampler.merge(summaries)
     launches = 4 * args.steps if args.impl == 'ours' else 0
     if rank == 0:
         rec = {

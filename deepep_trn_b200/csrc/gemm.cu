@@ -54,6 +54,8 @@ struct Args {
   int64_t ldh;
   int64_t c_group_stride;   // GROUP_K: elements between experts' outputs
   int64_t c_rows;           // GROUP_M: rows of C (and H); later tile rows are not stored
+  const void* R;            // GROUP_M bf16 epilogue: optional residual [rows, N] added before rounding
+  int64_t ldr;
   uint32_t* error;          // device word, non-zero after a timeout
   uint64_t timeout_ns;
 };
@@ -432,6 +434,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (EPI == kEpiF32) {
             store_box(&tmC, [&](uint8_t* sl) { put_row_f32(sl, lane, r); }, tl.n0 + c, row0, tl.g);
           } else {
+            if (!GROUP_K && a.R != nullptr && row0 + lane < a.c_rows) {
+              // residual row chunk (N % 32 == 0 is checked on the host), added in fp32
+              const int4* rr = reinterpret_cast<const int4*>(static_cast<const __nv_bfloat16*>(a.R) +
+                                                             static_cast<int64_t>(row0 + lane) * a.ldr + tl.n0 + c);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int4 q4 = rr[j];
+                const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&q4);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const float2 f = __bfloat1622float2(h2[i]);
+                  r[8 * j + 2 * i] = __float_as_uint(__uint_as_float(r[8 * j + 2 * i]) + f.x);
+                  r[8 * j + 2 * i + 1] = __float_as_uint(__uint_as_float(r[8 * j + 2 * i + 1]) + f.y);
+                }
+              }
+            }
             uint32_t v[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] = pack_bf16(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
@@ -548,7 +566,7 @@ void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
 // instead of [G, N, K].
 void grouped_gemm_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, const OptTensor& C,
                     const OptTensor& Hout, int64_t epilogue, at::Tensor error, int64_t num_sms, double timeout_s,
-                    bool b_kn) {
+                    bool b_kn, const OptTensor& residual) {
   using namespace gemm;
   const c10::cuda::CUDAGuard guard(A.device());
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "A, B must be bf16");
@@ -583,6 +601,14 @@ void grouped_gemm_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
     a.ldc = C->stride(0);
   } else {
     TORCH_CHECK(epilogue == kEpiSwiGLU, "C is required");
+  }
+  if (residual.has_value()) {
+    TORCH_CHECK(epilogue == kEpiBF16 && residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1 &&
+                    residual->size(0) >= a.c_rows && residual->size(1) == a.N && a.N % 32 == 0 &&
+                    (reinterpret_cast<uintptr_t>(residual->data_ptr()) & 15) == 0 && residual->stride(0) % 8 == 0,
+                "residual: bf16 [rows, N] with N % 32 == 0, 16-byte aligned rows, bf16 epilogue");
+    a.R = residual->data_ptr();
+    a.ldr = residual->stride(0);
   }
   // output maps: rows past A's (the padding of the last segment) are clipped by the map
   const CUtensorMap mh = epilogue == kEpiSwiGLU ? make_out_map(a.H, false, a.c_rows, a.N / 2, a.ldh, 0)

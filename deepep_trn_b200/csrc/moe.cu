@@ -15,6 +15,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <cstdlib>
+
 #include "ops.h"
 
 namespace b200ep {
@@ -222,8 +224,88 @@ __global__ void __launch_bounds__(256) permute_copy_kernel(const uint8_t* __rest
   }
 }
 
+// The same copy driven by the bulk-copy engine: one thread per CTA streams the CTA's
+// source rows into a ring of shared-memory stages (each row read once) and, as each
+// lands, issues one bulk store per destination slot (up to K). The other warps zero
+// the CTA's share of the padding rows meanwhile. Waits are bounded; a timed-out wait
+// sets *error, lets the loads in flight land and stops.
+constexpr int kPermCopyThreads = 128;
+constexpr int kPermCopyTok = 64;   // tokens per CTA pass (their pos rows are staged in smem)
+
+__global__ void __launch_bounds__(kPermCopyThreads) permute_copy_bulk_kernel(
+    const uint8_t* __restrict__ x, int64_t x_stride, int N, int K, int64_t row_bytes, const int32_t* __restrict__ pos,
+    uint8_t* __restrict__ out, const int64_t* __restrict__ offsets, const int32_t* __restrict__ counts, int EL,
+    int stage_bytes, int nstages, uint32_t* __restrict__ error, uint64_t timeout_ns) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + static_cast<int64_t>(nstages) * stage_bytes);
+  __shared__ int32_t s_pos[kPermCopyTok * 32];
+  const int tid = threadIdx.x;
+  const int n0 = static_cast<int>(static_cast<int64_t>(N) * blockIdx.x / gridDim.x);
+  const int n1 = static_cast<int>(static_cast<int64_t>(N) * (blockIdx.x + 1) / gridDim.x);
+  if (tid == 0) {
+    for (int i = 0; i < nstages; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+  }
+  uint32_t phase_bits = 0;
+  bool ok = true;
+  for (int c0 = n0; c0 < n1; c0 += kPermCopyTok) {
+    const int n = min(kPermCopyTok, n1 - c0);
+    __syncthreads();  // the previous pass is done with s_pos
+    for (int i = tid; i < n * K; i += kPermCopyThreads) s_pos[i] = pos[static_cast<int64_t>(c0) * K + i];
+    __syncthreads();
+    if (tid == 0 && ok) {
+      auto issue = [&](int q) {
+        const int st = q % nstages;
+        mbar_arrive_expect_tx(&bars[st], static_cast<uint32_t>(row_bytes));
+        bulk_load(smem + static_cast<int64_t>(st) * stage_bytes, x + static_cast<int64_t>(c0 + q) * x_stride,
+                  static_cast<uint32_t>(row_bytes), &bars[st]);
+      };
+      const int pro = min(n, nstages);
+      for (int q = 0; q < pro; ++q) issue(q);
+      for (int m = 0; m < n; ++m) {
+        const int st = m % nstages;
+        if (!mbar_wait(&bars[st], (phase_bits >> st) & 1u, timeout_ns)) {
+          atomicExch(error, 1u);
+          const int last = min(n - 1, m >= 1 ? m - 2 + nstages : pro - 1);
+          for (int q = m + 1; q <= last; ++q)
+            mbar_wait(&bars[q % nstages], (phase_bits >> (q % nstages)) & 1u, timeout_ns);
+          ok = false;
+          break;
+        }
+        phase_bits ^= 1u << st;
+        const uint8_t* src = smem + static_cast<int64_t>(st) * stage_bytes;
+        for (int k = 0; k < K; ++k) {
+          const int p = s_pos[m * K + k];
+          if (p >= 0) bulk_store(out + static_cast<int64_t>(p) * row_bytes, src, static_cast<uint32_t>(row_bytes));
+        }
+        bulk_commit();
+        const int q = m - 1 + nstages;
+        if (m >= 1 && q < n) {
+          bulk_wait_read<1>();  // the stores of token m - 1 have read their stage
+          issue(q);
+        }
+      }
+      bulk_wait_read<0>();
+    }
+  }
+  // padding rows of every segment: warps 1.. of all CTAs, plain 16-byte stores
+  const int warp = tid >> 5, lane = tid & 31;
+  constexpr int kZeroWarps = kPermCopyThreads / 32 - 1;
+  if (warp >= 1) {
+    const int gw = blockIdx.x * kZeroWarps + (warp - 1), GW = gridDim.x * kZeroWarps;
+    for (int e = 0; e < EL; ++e) {
+      const int64_t s0 = offsets[e] + counts[e], t = offsets[e + 1];
+      for (int64_t r = s0 + gw; r < t; r += GW) {
+        int4* d = reinterpret_cast<int4*>(out + r * row_bytes);
+        for (int64_t i = lane; i < row_bytes / 16; i += 32) d[i] = make_int4(0, 0, 0, 0);
+      }
+    }
+  }
+  if (tid == 0) bulk_wait<0>();  // the row stores are complete before the CTA exits
+}
+
 void permute(const at::Tensor& x, const at::Tensor& ids, int64_t num_local_experts, at::Tensor out, at::Tensor pos,
-             at::Tensor offsets, at::Tensor counts, at::Tensor scratch) {
+             at::Tensor offsets, at::Tensor counts, at::Tensor scratch, const OptTensor& error) {
   const c10::cuda::CUDAGuard guard(x.device());
   const int N = static_cast<int>(x.size(0)), K = static_cast<int>(ids.size(1)), EL = static_cast<int>(num_local_experts);
   TORCH_CHECK(EL <= kPermMaxExperts, "too many local experts");
@@ -249,10 +331,30 @@ void permute(const at::Tensor& x, const at::Tensor& ids, int64_t num_local_exper
                                                            pos.data_ptr<int32_t>());
   }
   const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
-  permute_copy_kernel<<<sms * 4, 256, 0, s>>>(static_cast<const uint8_t*>(x.data_ptr()), x.stride(0) * x.element_size(),
-                                              N, K, row_bytes, pos.data_ptr<int32_t>(),
-                                              static_cast<uint8_t*>(out.data_ptr()), offsets.data_ptr<int64_t>(),
-                                              counts.data_ptr<int32_t>(), EL);
+  const int64_t xs = x.stride(0) * x.element_size();
+  const uintptr_t xp = reinterpret_cast<uintptr_t>(x.data_ptr()), op = reinterpret_cast<uintptr_t>(out.data_ptr());
+  const bool bulk = error.has_value() && ((xp | op) & 15) == 0 && xs % 16 == 0 && row_bytes <= 65536 &&
+                    !std::getenv("B200EP_PERMUTE_WARPCOPY");
+  if (bulk) {
+    const int stage_bytes = static_cast<int>((row_bytes + 127) / 128 * 128);
+    const int nstages = static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(8, (96 * 1024) / stage_bytes)));
+    const size_t smem = static_cast<size_t>(nstages) * stage_bytes + nstages * 8;
+    static bool attr = false;
+    if (!attr) {
+      AT_CUDA_CHECK(cudaFuncSetAttribute(permute_copy_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024));
+      attr = true;
+    }
+    const int grid = std::max(1, std::min(N, sms * 2));
+    permute_copy_bulk_kernel<<<grid, kPermCopyThreads, smem, s>>>(
+        static_cast<const uint8_t*>(x.data_ptr()), xs, N, K, row_bytes, pos.data_ptr<int32_t>(),
+        static_cast<uint8_t*>(out.data_ptr()), offsets.data_ptr<int64_t>(), counts.data_ptr<int32_t>(), EL, stage_bytes,
+        nstages, reinterpret_cast<uint32_t*>(error->data_ptr<int32_t>()), 10ull * 1000 * 1000 * 1000);
+  } else {
+    permute_copy_kernel<<<sms * 4, 256, 0, s>>>(static_cast<const uint8_t*>(x.data_ptr()), xs, N, K, row_bytes,
+                                                pos.data_ptr<int32_t>(), static_cast<uint8_t*>(out.data_ptr()),
+                                                offsets.data_ptr<int64_t>(), counts.data_ptr<int32_t>(), EL);
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -102,8 +102,8 @@ class _MoEFunction(torch.autograd.Function):
         with timer.stage('moe.bwd.router'):
             dlogits = MO.router_topk_bwd(idx, w, dw.float(), ctx.num_experts).to(x.dtype)
             seg = _single_segment(x.shape[0], x.device)
-            dx_router = G.grouped_gemm(dlogits, Wr.unsqueeze(0), seg, epilogue='f32', b_layout='kn')  # [T, H]
-            dx = (dx.float() + dx_router).to(x.dtype)
+            # dx = combine's dx + dlogits @ Wr, summed in fp32 in the GEMM epilogue, one rounding
+            dx = G.grouped_gemm(dlogits, Wr.unsqueeze(0), seg, b_layout='kn', residual=dx.contiguous())
             if ctx.num_experts % 64 == 0:
                 dWr = G.grouped_gemm_wgrad(dlogits, x, seg, out_dtype=Wr.dtype)[0]            # [E, H]
             else:  # the token-major operand path tiles M in 64-wide atoms
@@ -127,14 +127,20 @@ class MoELayer(nn.Module):
         self.hidden, self.intermediate = hidden, intermediate
         self.num_experts, self.topk = num_experts, topk
         EL = num_experts // R
-        g = torch.Generator().manual_seed(seed)
-        g_local = torch.Generator().manual_seed(seed * 1000 + buffer.rank + 1)
+        # seeded on the target device (the router is shared by all ranks, the experts are per rank)
+        gdev = torch.device(device) if device is not None else torch.device('cpu')
+        g = torch.Generator(device=gdev).manual_seed(seed)
+        g_local = torch.Generator(device=gdev).manual_seed(seed * 1000 + buffer.rank + 1)
         std = init_std
-        self.router = nn.Parameter((torch.randn(num_experts, hidden, generator=g) * std).to(dtype).to(device))
-        wg = torch.randn(EL, intermediate, hidden, generator=g_local) * std
-        wu = torch.randn(EL, intermediate, hidden, generator=g_local) * std
-        self.w1 = nn.Parameter(G.interleave_gate_up(wg, wu).to(dtype).to(device))
-        self.w2 = nn.Parameter((torch.randn(EL, hidden, intermediate, generator=g_local) * std).to(dtype).to(device))
+
+        def randn(*shape, gen):
+            return (torch.randn(*shape, generator=gen, device=gdev) * std).to(dtype)
+        self.router = nn.Parameter(randn(num_experts, hidden, gen=g))
+        wg = randn(EL, intermediate, hidden, gen=g_local)
+        wu = randn(EL, intermediate, hidden, gen=g_local)
+        self.w1 = nn.Parameter(G.interleave_gate_up(wg, wu))
+        del wg, wu
+        self.w2 = nn.Parameter(randn(EL, hidden, intermediate, gen=g_local))
         # fp32 bias added to the router logits before top-k (not trained here; it steers load,
         # e.g. a Zipf skew for benchmarks or a balancing bias)
         self.register_buffer('router_bias', torch.zeros(num_experts, dtype=torch.float32, device=device))

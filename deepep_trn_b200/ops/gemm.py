@@ -35,25 +35,28 @@ def check(device=None) -> None:
     e = _err(dev)
     if int(e.item()):
         e.zero_()
-        raise RuntimeError('grouped GEMM: a pipeline wait timed out on the device')
+        raise RuntimeError("a grouped GEMM or permute kernel gave up on a timed-out wait on the device")
 
 
 def grouped_gemm(A: torch.Tensor, B: torch.Tensor, offsets: torch.Tensor, out: torch.Tensor | None = None,
                  epilogue: str = 'bf16', h_out: torch.Tensor | None = None, save_preact: bool = True,
-                 num_sms: int = 0, timeout_s: float = 10.0, b_layout: str = 'nk'):
+                 num_sms: int = 0, timeout_s: float = 10.0, b_layout: str = 'nk',
+                 residual: torch.Tensor | None = None):
     """Returns C (or ``(h, pre_activation)`` for ``epilogue='swiglu'``). ``b_layout='kn'``
-    takes B as [G, K, N] (e.g. a forward weight, for the input gradient)."""
+    takes B as [G, K, N] (e.g. a forward weight, for the input gradient). ``residual``
+    (bf16 [rows, N], bf16 epilogue only) is added to the fp32 accumulator before rounding."""
     kn = b_layout == 'kn'
     rows, N = A.shape[0], B.shape[2 if kn else 1]
     if epilogue == 'swiglu':
         h = h_out if h_out is not None else torch.empty(rows, N // 2, dtype=torch.bfloat16, device=A.device)
         c = (out if out is not None else torch.empty(rows, N, dtype=torch.bfloat16, device=A.device)) \
             if save_preact else None
-        load().grouped_gemm_m(A, B, offsets, c, h, 2, _err(A.device), num_sms, timeout_s, kn)
+        load().grouped_gemm_m(A, B, offsets, c, h, 2, _err(A.device), num_sms, timeout_s, kn, None)
         return h, c
     dtype = torch.float32 if epilogue == 'f32' else torch.bfloat16
     c = out if out is not None else torch.empty(rows, N, dtype=dtype, device=A.device)
-    load().grouped_gemm_m(A, B, offsets, c, None, EPILOGUES[epilogue], _err(A.device), num_sms, timeout_s, kn)
+    load().grouped_gemm_m(A, B, offsets, c, None, EPILOGUES[epilogue], _err(A.device), num_sms, timeout_s, kn,
+                          residual)
     return c
 
 

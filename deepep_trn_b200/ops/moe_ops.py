@@ -74,7 +74,8 @@ def permute(x: torch.Tensor, local_ids: torch.Tensor, num_local_experts: int, co
     cnt = torch.empty(EL, dtype=torch.int32, device=dev)
     nblocks = max(1, (N + 31) // 32)
     scratch = torch.empty(nblocks * EL, dtype=torch.int32, device=dev)
-    load().permute(x, local_ids.contiguous(), EL, rows, pos, offsets, cnt, scratch)
+    from .gemm import _err  # the kernels' shared device error word (timed-out copies)
+    load().permute(x, local_ids.contiguous(), EL, rows, pos, offsets, cnt, scratch, _err(dev))
     return rows, pos, offsets, cnt
 
 

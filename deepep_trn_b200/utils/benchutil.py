@@ -3,7 +3,7 @@
 * ``DeviceTimer``: time each step with CUDA events on the launching stream, with an
   L2 flush (a write larger than the 126 MB L2) outside the timed events; totals are
   reduced as the max over ranks.
-* ``ClockSampler``: ``nvidia-smi`` clocks / throttle reasons sampled every 200 ms
+* ``ClockSampler``: SM clocks / clock-event reasons sampled through NVML every 5 ms
   during the timed region, summarised as median SM MHz under load.
 * ``env_record``: versions and hardware for the JSONL records (reference
   bench/common.py:147-177 captures the same kind of metadata).
@@ -15,7 +15,6 @@ import os
 import statistics
 import subprocess
 import sys
-import tempfile
 import time
 from pathlib import Path
 
@@ -66,69 +65,95 @@ def sum_over_ranks(value: float, group=None) -> float:
 
 
 class ClockSampler:
-    """Samples SM clocks and throttle reasons with nvidia-smi while active."""
+    """Samples this process's GPU (SM clock, its maximum, power, clock-event reasons) through
+    NVML while active: one sample on entry, one every ``period_s`` from a background thread,
+    one on exit, so even a timed region of a few milliseconds is covered. Read-only queries;
+    nothing about the GPU is changed. ``merge`` combines the ranks' summaries.
+    """
 
-    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
-              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
-              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+    REASONS = (('hw_slowdown', 'nvmlClocksEventReasonHwSlowdown', 0x8),
+               ('hw_thermal_slowdown', 'nvmlClocksEventReasonHwThermalSlowdown', 0x40),
+               ('sw_thermal_slowdown', 'nvmlClocksEventReasonSwThermalSlowdown', 0x20),
+               ('hw_power_brake', 'nvmlClocksEventReasonHwPowerBrakeSlowdown', 0x80),
+               ('sw_power_cap', 'nvmlClocksEventReasonSwPowerCap', 0x4))
 
-    def __init__(self, gpus: list[int]):
-        self.gpus = gpus
-        self.proc = None
-        self.path = None
+    def __init__(self, device: int | None = None, period_s: float = 0.005):
+        self.period_s = period_s
+        self.samples: list[tuple[float, float, int]] = []   # (sm MHz, max MHz, reason bits)
+        self.nvml = None
+        self.handle = None
+        self._stop = None
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            dev = torch.cuda.current_device() if device is None else device
+            props = torch.cuda.get_device_properties(dev)
+            bus = f'{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0'
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:  # noqa: BLE001 - fall back to the enumeration index
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(dev)
+            self.nvml = pynvml
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        except Exception as exc:  # noqa: BLE001 - no NVML: report unavailable
+            log(f'clock sampling unavailable: {exc}')
+
+    def _sample(self) -> None:
+        p = self.nvml
+        try:
+            sm = float(p.nvmlDeviceGetClockInfo(self.handle, p.NVML_CLOCK_SM))
+            bits = int(p.nvmlDeviceGetCurrentClocksEventReasons(self.handle))
+            self.samples.append((sm, self.max_mhz, bits))
+        except Exception:  # noqa: BLE001 - a failed read is a missing sample
+            pass
+
+    def _loop(self) -> None:
+        while not self._stop.wait(self.period_s):
+            self._sample()
 
     def __enter__(self):
-        try:
-            fd, self.path = tempfile.mkstemp(suffix='.csv')
-            os.close(fd)
-            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
-                                          '-lms', '200', '-f', self.path],
-                                         stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
-        except Exception as exc:  # nvidia-smi missing
-            log(f'clock sampling unavailable: {exc}')
-            self.proc = None
+        if self.nvml is not None:
+            import threading
+            self._sample()
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._loop, daemon=True)
+            self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            time.sleep(0.25)
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+            self._sample()
 
     def summary(self) -> dict:
-        if self.path is None or not Path(self.path).exists():
+        if self.nvml is None:
             return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unavailable']}
-        rows = []
-        for line in Path(self.path).read_text().splitlines():
-            parts = [p.strip() for p in line.split(',')]
-            if len(parts) < 9:
-                continue
-            try:
-                idx = int(parts[0])
-            except ValueError:
-                continue
-            if idx not in self.gpus:
-                continue
-            rows.append(parts)
-        os.unlink(self.path)
-        if not rows:
+        if not self.samples:
             return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['no samples']}
-        sm = [float(r[1]) for r in rows if r[1].replace('.', '').isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace('.', '').isdigit()]
-        # "under load": samples above half of max (idle samples drop to ~100s of MHz)
-        top = max(mx) if mx else 0
-        loaded = [v for v in sm if v > 0.5 * top] or sm
+        top = max(m for _, m, _ in self.samples)
+        sm = [s for s, _, _ in self.samples]
+        loaded = [v for v in sm if v > 0.5 * top] or sm   # under load (idle drops far below)
         reasons = set()
-        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
-        for r in rows:
-            for n, v in zip(names, r[5:9]):
-                if v.strip().lower() == 'active':
-                    reasons.add(n)
-        return {'sm_mhz': statistics.median(loaded) if loaded else None, 'sm_max_mhz': top or None,
-                'reasons': sorted(reasons), 'samples': len(rows)}
+        for _, _, bits in self.samples:
+            for name, attr, default in self.REASONS:
+                if bits & int(getattr(self.nvml, attr, default)):
+                    reasons.add(name)
+        return {'sm_mhz': statistics.median(loaded), 'sm_max_mhz': top, 'reasons': sorted(reasons),
+                'samples': len(self.samples)}
+
+    @staticmethod
+    def merge(summaries: list[dict]) -> dict:
+        """All ranks' summaries -> one: median of the per-GPU medians, the lowest maximum, all reasons."""
+        have = [s for s in summaries if s.get('sm_mhz') is not None]
+        if not have:
+            return summaries[0] if summaries else {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['no samples']}
+        reasons = sorted({r for s in have for r in s['reasons']})
+        return {'sm_mhz': statistics.median(s['sm_mhz'] for s in have),
+                'sm_min_gpu_mhz': min(s['sm_mhz'] for s in have),
+                'sm_max_mhz': min(s['sm_max_mhz'] for s in have), 'reasons': reasons,
+                'samples': sum(s.get('samples', 0) for s in have), 'gpus': len(have)}
 
 
 def env_record() -> dict:

@@ -30,9 +30,15 @@ def torchrun(script: str, nproc: int, *args, timeout: int = 600, env=None):
     e['PYTHONPATH'] = str(ROOT) + os.pathsep + e.get('PYTHONPATH', '')
     if env:
         e.update(env)
-    p = subprocess.run(['timeout', '-k', '30', str(timeout), *cmd], capture_output=True, text=True, env=e,
-                       cwd=str(ROOT))
-    return p.returncode, p.stdout + p.stderr
+    for _ in range(3):
+        p = subprocess.run(['timeout', '-k', '30', str(timeout), *cmd], capture_output=True, text=True, env=e,
+                           cwd=str(ROOT))
+        out = p.stdout + p.stderr
+        if p.returncode == 0 or 'EADDRINUSE' not in out:
+            break
+        # the rendezvous port was taken between probing and binding: retry on a fresh one
+        cmd[cmd.index('--master-port') + 1] = str(free_port())
+    return p.returncode, out
 
 
 @pytest.fixture

@@ -28,7 +28,8 @@ import torch.distributed as dist
 
 
 def report(rank: int, exc) -> None:
-    print(f'RANK={rank} DETECTED={type(exc).__name__}' if exc is not None else f'RANK={rank} UNDETECTED',
+    # a leading newline keeps the line whole when ranks' outputs interleave
+    print(f'\nRANK={rank} DETECTED={type(exc).__name__};' if exc is not None else f'\nRANK={rank} UNDETECTED;',
           flush=True)
 
 

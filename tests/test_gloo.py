@@ -80,7 +80,7 @@ def test_host_made_failures_raise(run_dist, case):
     """Failures made on the host end in exceptions on the ranks that can see them, not in hangs."""
     import re
     rc, out = run_dist('failures.py', 3, '--case', case, timeout=240, env={'B200EP_PG_TIMEOUT': '20'})
-    lines = re.findall(r'RANK=(\d+) (DETECTED=\w+|UNDETECTED)', out)
+    lines = re.findall(r'RANK=(\d+) (DETECTED=\w+?|UNDETECTED);', out)
     status = {int(r): s for r, s in lines}
     if case == 'config':
         assert rc == 0 and all(status.get(r) == 'DETECTED=ValueError' for r in range(3)), out[-3000:]

@@ -115,3 +115,19 @@ def test_grouped_gemm_b_kn(G, counts, N, K):
     for e in range(G):
         s, t = offs[e], offs[e] + counts[e]
         _close(C[s:t], A[s:t].float() @ B[e].float())
+
+
+@needs_cuda
+def test_grouped_gemm_residual_epilogue():
+    # C = A @ B + R with the sum taken in fp32 before the one bf16 rounding
+    from deepep_trn_b200.ops.gemm import check, grouped_gemm
+    torch.manual_seed(4)
+    T, K, N = 300, 256, 7168
+    A = (torch.randn(T, K, device='cuda') * 0.5).to(torch.bfloat16)
+    B = (torch.randn(1, K, N, device='cuda') * 0.05).to(torch.bfloat16)
+    R = torch.randn(T, N, device='cuda').to(torch.bfloat16)
+    o = torch.tensor([0, (T + 127) // 128 * 128], dtype=torch.int64, device='cuda')
+    C = grouped_gemm(A, B, o, b_layout='kn', residual=R)
+    torch.cuda.synchronize()
+    check()
+    _close(C, A.float() @ B[0].float() + R.float(), tol=1e-2)
