@@ -829,8 +829,14 @@ struct NcPullArgs {
   int nstages, stage_bytes;
 };
 
-constexpr int kPullTok = 16;   // tokens per batch (one warp builds each token's row list)
+constexpr int kPullTok = 32;        // tokens per batch (their row lists are built together)
+constexpr int kPullConsumers = kCombThreads / 32 - 1;   // warp 0 drives the loads, the rest reduce
 
+// Row stream of the pull combine. Warp 0's lane 0 issues one bulk load per row into a ring
+// of shared-memory stages (full barrier: transaction bytes; empty barrier: one arrival
+// per consumer warp); warps 1.. each own fixed 16-byte chunks of the row, accumulate
+// in fp32 and store a token's output after its last row, without CTA-wide barriers
+// between rows.
 template <typename T16>
 __global__ void __launch_bounds__(kCombThreads) nc_pull_kernel(NcPullArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_ring[];
@@ -844,13 +850,18 @@ __global__ void __launch_bounds__(kCombThreads) nc_pull_kernel(NcPullArgs a) {
   const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
   constexpr int nwarps = kCombThreads / 32;
   const int gw = blockIdx.x * nwarps + warp, GW = gridDim.x * nwarps;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_ring + static_cast<int64_t>(a.nstages) * a.stage_bytes);
+  const int ns = a.nstages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_ring + static_cast<int64_t>(ns) * a.stage_bytes);
+  uint64_t* empty = full + ns;
 
   __shared__ int64_t s_off[B200EP_MAX_RANKS + 1];
   __shared__ int64_t s_roff[B200EP_MAX_RANKS];
-  __shared__ int s_last, s_fail;
-  __shared__ const uint8_t* s_src[kPullTok * B200EP_MAX_RANKS];
-  __shared__ int16_t s_n[kPullTok + 1];
+  __shared__ int s_last;
+  __shared__ volatile int s_fail;
+  __shared__ const uint8_t* s_rows[kPullTok * B200EP_MAX_RANKS];  // the batch's rows, token-major
+  __shared__ int16_t s_rtok[kPullTok * B200EP_MAX_RANKS];         // token of the row if it is its last, else -1
+  __shared__ int s_cnt[kPullTok];
+  __shared__ int s_n[kPullTok + 1];
   if (tid <= R) s_off[tid] = a.recv_off[tid];
   if (blockIdx.x == 0 && tid == 0) ls->trace[kTrCombStart] = global_ns();
   __syncthreads();
@@ -895,7 +906,10 @@ __global__ void __launch_bounds__(kCombThreads) nc_pull_kernel(NcPullArgs a) {
   if (s_fail) return;
   if (blockIdx.x == 0 && tid == 0) ls->trace[kTrCombPeersReady] = global_ns();
   if (tid == 0) {
-    for (int st = 0; st < a.nstages; ++st) mbar_init(&bars[st], 1);
+    for (int st = 0; st < ns; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], kPullConsumers);
+    }
     fence_mbar_init();
     fence_proxy_async_global();
   }
@@ -905,24 +919,22 @@ __global__ void __launch_bounds__(kCombThreads) nc_pull_kernel(NcPullArgs a) {
   const int nch = H / 8;                           // 16-byte chunks per row
   const int t0 = static_cast<int>(static_cast<int64_t>(a.T) * blockIdx.x / gridDim.x);
   const int t1 = static_cast<int>(static_cast<int64_t>(a.T) * (blockIdx.x + 1) / gridDim.x);
-  uint32_t g = 0;  // rows consumed so far by this CTA (drives stage and parity)
-  for (int tb = t0; tb < t1; tb += kPullTok) {
+  uint32_t g = 0;  // rows streamed so far by this CTA (drives stage and parity)
+  for (int tb = t0; tb < t1 && !s_fail; tb += kPullTok) {
     const int nt = min(kPullTok, t1 - tb);
-    // row list of the batch, in (token, rank) order
-    if (warp < nt) {
-      const int t = tb + warp;
+    // per token: its rows (one per rank it visited) and its combined weights
+    int pv[kPullTok / nwarps];
+#pragma unroll
+    for (int u = 0; u < kPullTok / nwarps; ++u) {
+      const int i = warp + u * nwarps;
+      pv[u] = -1;
+      if (i >= nt) continue;
+      const int t = tb + i;
       const int p = lane < R ? a.token_pos[static_cast<int64_t>(t) * R + lane] : -1;
-      const uint32_t b = __ballot_sync(0xffffffffu, p >= 0);
-      if (lane == 0) s_n[warp + 1] = static_cast<int16_t>(__popc(b));
-      __syncwarp();
-      if (p >= 0) {
-        const int q = __popc(b & lanemask_lt());
-        s_src[warp * B200EP_MAX_RANKS + q] =
-            lane == me ? a.x + (s_off[me] + p) * a.x_stride
-                       : hv.base[lane] + hv.L.nc_send[slot] + (s_roff[lane] + p) * RB;
-      }
+      pv[u] = p;
+      const uint32_t bt = __ballot_sync(0xffffffffu, p >= 0);  // every lane takes part
+      if (lane == 0) s_cnt[i] = __popc(bt);
       if (a.out_w) {
-        // combined weights: sum over the ranks the token visited
         float acc_w = 0.f;
         for (int r = 0; r < R; ++r) {
           const int pr = __shfl_sync(0xffffffffu, p, r);
@@ -935,94 +947,129 @@ __global__ void __launch_bounds__(kCombThreads) nc_pull_kernel(NcPullArgs a) {
       }
     }
     __syncthreads();
-    if (tid == 0) {
-      s_n[0] = 0;
-      for (int i = 0; i < nt; ++i) s_n[i + 1] = static_cast<int16_t>(s_n[i] + s_n[i + 1]);
+    if (warp == 0) {  // exclusive scan of the row counts
+      const int c = lane < nt ? s_cnt[lane] : 0;
+      int v = c;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += o;
+      }
+      s_n[lane] = v - c;
+      if (lane == 31) s_n[kPullTok] = v;
     }
     __syncthreads();
-    const int nrows = s_n[nt];
-    // compact the list: rows of token i sit at [s_n[i], s_n[i+1])
-    auto row_src = [&](int k) -> const uint8_t* {
-      int i = 0;
-      while (s_n[i + 1] <= k) ++i;
-      return s_src[i * B200EP_MAX_RANKS + (k - s_n[i])];
-    };
-    auto issue = [&](int k, uint32_t gk) {
-      const int st = static_cast<int>(gk % a.nstages);
-      mbar_arrive_expect_tx(&bars[st], static_cast<uint32_t>(RB));
-      bulk_load(smem_ring + static_cast<int64_t>(st) * a.stage_bytes, row_src(k), static_cast<uint32_t>(RB), &bars[st]);
-    };
-    if (tid == 0)
-      for (int k = 0; k < nrows && k < a.nstages; ++k) issue(k, g + k);
-    float acc[4][8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < kPullTok / nwarps; ++u) {
+      const int i = warp + u * nwarps;
+      if (i >= nt) continue;
+      const int p = pv[u];
+      const uint32_t b = __ballot_sync(0xffffffffu, p >= 0);
+      if (p >= 0) {
+        const int q = __popc(b & lanemask_lt());
+        const int k = s_n[i] + q;
+        s_rows[k] = lane == me ? a.x + (s_off[me] + p) * a.x_stride
+                               : hv.base[lane] + hv.L.nc_send[slot] + (s_roff[lane] + p) * RB;
+        s_rtok[k] = static_cast<int16_t>(q == __popc(b) - 1 ? i : -1);
+      }
+    }
+    __syncthreads();
+    const int nrows = s_n[kPullTok];
+
+    if (warp == 0) {
+      // ------------------------------------------------------------ producer
+      if (lane == 0) {
+        int k = 0;
+        for (; k < nrows; ++k) {
+          const uint32_t gk = g + k;
+          const int st = static_cast<int>(gk % ns);
+          if (gk >= static_cast<uint32_t>(ns) &&
+              !mbar_wait(&empty[st], ((gk / ns) + 1u) & 1u, hv.timeout_ns)) {
+            s_fail = 1;
+            break;
+          }
+          if (s_fail) break;
+          mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(RB));
+          bulk_load(smem_ring + static_cast<int64_t>(st) * a.stage_bytes, s_rows[k], static_cast<uint32_t>(RB),
+                    &full[st]);
+        }
+        if (s_fail) {
+          // let the loads still in flight land before the CTA's shared memory is released
+          for (int kk = max(0, k - ns); kk < k; ++kk) {
+            const uint32_t gk = g + kk;
+            mbar_wait(&full[gk % ns], (gk / ns) & 1u, hv.timeout_ns);
+          }
+        }
+      }
+    } else {
+      // ------------------------------------------------------------ consumers
+      const int ct = tid - 32;                   // 0 .. 32 * kPullConsumers - 1
+      constexpr int CT = 32 * kPullConsumers;
+      float acc[4][8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[u][i] = 0.f;
-    int tok = 0;
-    for (int k = 0; k < nrows; ++k, ++g) {
-      const int st = static_cast<int>(g % a.nstages);
-      // a timed-out thread skips the row and raises s_fail; every thread still reaches the
-      // barrier below, and the whole CTA stops after it
-      if (mbar_wait(&bars[st], (g / a.nstages) & 1u, hv.timeout_ns)) {
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[u][q] = 0.f;
+      for (int k = 0; k < nrows; ++k) {
+        const uint32_t gk = g + k;
+        const int st = static_cast<int>(gk % ns);
+        if (!mbar_wait(&full[st], (gk / ns) & 1u, hv.timeout_ns)) {
+          s_fail = 1;
+          break;
+        }
+        if (s_fail) break;
         const uint8_t* row = smem_ring + static_cast<int64_t>(st) * a.stage_bytes;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int j = tid + u * kCombThreads;
+          const int j = ct + u * CT;
           if (j < nch) acc8<T16>(acc[u], *reinterpret_cast<const int4*>(row + j * 16));
         }
-      } else {
-        s_fail = 1;
-      }
-      while (s_n[tok + 1] <= k) ++tok;
-      if (k + 1 == s_n[tok + 1]) {
-        // last row of this token: bias, cast, store, reset
-        const int64_t t = tb + tok;
-        T16* out = reinterpret_cast<T16*>(a.out) + t * H;
+        __syncwarp();
+        if (lane == 0) mbar_arrive_local(&empty[st]);
+        const int i = s_rtok[k];
+        if (i >= 0) {
+          // last row of token i: bias, cast, store, reset
+          const int64_t t = tb + i;
+          T16* out = reinterpret_cast<T16*>(a.out) + t * H;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int j = tid + u * kCombThreads;
-          if (j >= nch) continue;
-          if (a.bias0) acc8<T16>(acc[u], reinterpret_cast<const int4*>(a.bias0 + t * RB)[j]);
-          if (a.bias1) acc8<T16>(acc[u], reinterpret_cast<const int4*>(a.bias1 + t * RB)[j]);
+          for (int u = 0; u < 4; ++u) {
+            const int j = ct + u * CT;
+            if (j >= nch) continue;
+            if (a.bias0) acc8<T16>(acc[u], reinterpret_cast<const int4*>(a.bias0 + t * RB)[j]);
+            if (a.bias1) acc8<T16>(acc[u], reinterpret_cast<const int4*>(a.bias1 + t * RB)[j]);
+            int4 o;
+            T16* oh = reinterpret_cast<T16*>(&o);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) oh[q] = static_cast<T16>(acc[u][q]);
+            reinterpret_cast<int4*>(out)[j] = o;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) acc[u][q] = 0.f;
+          }
+        }
+      }
+      // tokens routed nowhere (all top-k masked) still get bias (or zeros)
+      for (int i = warp - 1; i < nt; i += kPullConsumers) {
+        if (s_cnt[i] != 0) continue;
+        const int64_t t = tb + i;
+        T16* out = reinterpret_cast<T16*>(a.out) + t * H;
+        for (int j = lane; j < nch; j += 32) {
+          float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if (a.bias0) acc8<T16>(z, reinterpret_cast<const int4*>(a.bias0 + t * RB)[j]);
+          if (a.bias1) acc8<T16>(z, reinterpret_cast<const int4*>(a.bias1 + t * RB)[j]);
           int4 o;
           T16* oh = reinterpret_cast<T16*>(&o);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) oh[i] = static_cast<T16>(acc[u][i]);
+          for (int q = 0; q < 8; ++q) oh[q] = static_cast<T16>(z[q]);
           reinterpret_cast<int4*>(out)[j] = o;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) acc[u][i] = 0.f;
         }
       }
-      __syncthreads();  // every thread is done with stage st
-      if (s_fail) {
-        if (tid == 0) {
-          report_error(hv.status, kTimeoutCombine, 3, me, -1, 0, 0, 2);
-          // let the loads still in flight land before the CTA's shared memory is released
-          for (int kk = k + 1; kk < nrows && kk < k + a.nstages; ++kk)
-            mbar_wait(&bars[(g + kk - k) % a.nstages], ((g + kk - k) / a.nstages) & 1u, hv.timeout_ns);
-        }
-        return;
-      }
-      if (tid == 0 && k + a.nstages < nrows) issue(k + a.nstages, g + a.nstages);
     }
-    // tokens routed nowhere (all top-k masked) still get bias (or zeros)
-    for (int i = warp; i < nt; i += nwarps) {
-      if (s_n[i + 1] != s_n[i]) continue;
-      const int64_t t = tb + i;
-      T16* out = reinterpret_cast<T16*>(a.out) + t * H;
-      for (int j = lane; j < nch; j += 32) {
-        float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (a.bias0) acc8<T16>(z, reinterpret_cast<const int4*>(a.bias0 + t * RB)[j]);
-        if (a.bias1) acc8<T16>(z, reinterpret_cast<const int4*>(a.bias1 + t * RB)[j]);
-        int4 o;
-        T16* oh = reinterpret_cast<T16*>(&o);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) oh[q] = static_cast<T16>(z[q]);
-        reinterpret_cast<int4*>(out)[j] = o;
-      }
-    }
-    __syncthreads();
+    g += static_cast<uint32_t>(nrows);
+    __syncthreads();  // the batch's lists are free again
+  }
+  if (s_fail) {
+    if (tid == 0) report_error(hv.status, kTimeoutCombine, 3, me, -1, 0, 0, 2);
+    return;
   }
   __syncthreads();
   if (tid == 0 && atomicAdd(&ls->arrive2[kEpNC], 1u) == gridDim.x - 1) {
@@ -1072,7 +1119,7 @@ void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const a
   void* kfn = x.scalar_type() == at::kHalf ? reinterpret_cast<void*>(nc_combine_kernel<__half>)
                                            : reinterpret_cast<void*>(nc_combine_kernel<__nv_bfloat16>);
   const uintptr_t xp = reinterpret_cast<uintptr_t>(a.x);
-  const bool aligned = (xp & 15) == 0 && (a.x_stride % 16) == 0 && (a.H % 8) == 0 && a.H <= 4 * 8 * kCombThreads;
+  const bool aligned = (xp & 15) == 0 && (a.x_stride % 16) == 0 && (a.H % 8) == 0 && a.H <= 4 * 8 * 32 * kPullConsumers;
   if (aligned && !getenv("B200EP_COMBINE_PUSH")) {
     NcPullArgs p{};
     p.hv = a.hv;
@@ -1091,7 +1138,7 @@ void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const a
     p.K = a.K;
     p.stage_bytes = static_cast<int>(align_up(2LL * a.H, 128));
     p.nstages = static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(12, (176 * 1024) / p.stage_bytes)));
-    const size_t psmem = static_cast<size_t>(p.nstages) * p.stage_bytes + p.nstages * 8;
+    const size_t psmem = static_cast<size_t>(p.nstages) * p.stage_bytes + p.nstages * 16;
     void* pfn = x.scalar_type() == at::kHalf ? reinterpret_cast<void*>(nc_pull_kernel<__half>)
                                              : reinterpret_cast<void*>(nc_pull_kernel<__nv_bfloat16>);
     static bool pattr[2] = {false, false};
