@@ -35,6 +35,7 @@ def main():
     p.add_argument('--warmup', type=int, default=3)
     p.add_argument('--impls', default='ours,nccl')
     p.add_argument('--breakdown', action='store_true', help='per-phase device time of the fused layer')
+    p.add_argument('--fp8', action='store_true', help='fused layer: forward dispatch in fp8 e4m3 + 1x128 scales')
     p.set_defaults(tokens=[4096])
     args = p.parse_args()
     T = args.tokens[0]
@@ -49,7 +50,7 @@ def main():
     for impl in args.impls.split(','):
         buf = Buffer(ctx.ep_group, backend='nvlink' if impl == 'ours' else 'nccl', num_max_tokens_per_rank=T,
                      hidden=H, num_experts=E, topk=K)
-        layer = (MoELayer(buf, H, I, E, K, device=dev, init_std=0.02, seed=7) if impl == 'ours'
+        layer = (MoELayer(buf, H, I, E, K, device=dev, init_std=0.02, seed=7, fp8_dispatch=args.fp8) if impl == 'ours'
                  else BaselineMoELayer(buf, H, I, E, K, device=dev))
         with torch.no_grad():
             if params is None:
@@ -103,7 +104,8 @@ def main():
         buf.destroy()
         del layer
         torch.cuda.empty_cache()
-    rec = dict(bench='moe', ep=ctx.ep, tokens=T, hidden=H, inter=I, experts=E, topk=K, routing='zipf', **results)
+    rec = dict(bench='moe', ep=ctx.ep, tokens=T, hidden=H, inter=I, experts=E, topk=K, routing='zipf',
+               dispatch_dtype='fp8-e4m3-1x128' if args.fp8 else 'bf16', **results)
     if 'ours' in results and 'nccl' in results:
         rec['speedup_vs_nccl_cublas'] = round(results['nccl']['ms_per_step'] / results['ours']['ms_per_step'], 3)
     if ctx.rank == 0:

@@ -304,8 +304,60 @@ __global__ void __launch_bounds__(kPermCopyThreads) permute_copy_bulk_kernel(
   if (tid == 0) bulk_wait<0>();  // the row stores are complete before the CTA exits
 }
 
+// fp8 input (e4m3 rows with one fp32 scale per 128 channels, as an fp8 dispatch delivers
+// them): a warp per token reads the row once, dequantises 16 channels per lane-chunk to
+// bf16 and stores them to every destination slot of the token.
+__global__ void __launch_bounds__(256) permute_copy_fp8_kernel(const uint8_t* __restrict__ q, int64_t q_stride,
+                                                               const float* __restrict__ sc, int64_t s_stride, int N,
+                                                               int K, int H, const int32_t* __restrict__ pos,
+                                                               __nv_bfloat16* __restrict__ out,
+                                                               const int64_t* __restrict__ offsets,
+                                                               const int32_t* __restrict__ counts, int EL) {
+  const int lane = lane_id();
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int GW = (gridDim.x * blockDim.x) >> 5;
+  const int nch = H / 16;  // 16 fp8 channels per chunk
+  for (int n = gw; n < N; n += GW) {
+    int p[32];
+    int np = 0;
+    for (int k = 0; k < K; ++k) {
+      const int v = pos[static_cast<int64_t>(n) * K + k];
+      if (v >= 0) p[np++] = v;
+    }
+    if (np == 0) continue;
+    const uint8_t* qr = q + static_cast<int64_t>(n) * q_stride;
+    const float* sr = sc + static_cast<int64_t>(n) * s_stride;
+    for (int j = lane; j < nch; j += 32) {
+      const int4 v = reinterpret_cast<const int4*>(qr)[j];
+      const float f = sr[j >> 3];  // 8 chunks of 16 per 128-channel block
+      const __nv_fp8x2_storage_t* b2 = reinterpret_cast<const __nv_fp8x2_storage_t*>(&v);
+      alignas(16) __nv_bfloat162 o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const __half2 h = __half2(__nv_cvt_fp8x2_to_halfraw2(b2[i], __NV_E4M3));
+        const float2 x2 = __half22float2(h);
+        o[i] = __floats2bfloat162_rn(x2.x * f, x2.y * f);
+      }
+      for (int i = 0; i < np; ++i) {
+        int4* d = reinterpret_cast<int4*>(out + static_cast<int64_t>(p[i]) * H) + 2 * j;
+        d[0] = reinterpret_cast<const int4*>(o)[0];
+        d[1] = reinterpret_cast<const int4*>(o)[1];
+      }
+    }
+  }
+  const int64_t row_bytes = 2LL * H;
+  for (int e = 0; e < EL; ++e) {
+    const int64_t s0 = offsets[e] + counts[e], t = offsets[e + 1];
+    for (int64_t r = s0 + gw; r < t; r += GW) {
+      int4* d = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(out) + r * row_bytes);
+      for (int64_t i = lane; i < row_bytes / 16; i += 32) d[i] = make_int4(0, 0, 0, 0);
+    }
+  }
+}
+
 void permute(const at::Tensor& x, const at::Tensor& ids, int64_t num_local_experts, at::Tensor out, at::Tensor pos,
-             at::Tensor offsets, at::Tensor counts, at::Tensor scratch, const OptTensor& error) {
+             at::Tensor offsets, at::Tensor counts, at::Tensor scratch, const OptTensor& error,
+             const OptTensor& x_scales) {
   const c10::cuda::CUDAGuard guard(x.device());
   const int N = static_cast<int>(x.size(0)), K = static_cast<int>(ids.size(1)), EL = static_cast<int>(num_local_experts);
   TORCH_CHECK(EL <= kPermMaxExperts, "too many local experts");
@@ -331,6 +383,19 @@ void permute(const at::Tensor& x, const at::Tensor& ids, int64_t num_local_exper
                                                            pos.data_ptr<int32_t>());
   }
   const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  if (x_scales.has_value()) {
+    TORCH_CHECK(x.element_size() == 1 && out.scalar_type() == at::kBFloat16 && out.size(1) == x.size(1) &&
+                    x.size(1) % 128 == 0 && x_scales->scalar_type() == at::kFloat && x_scales->stride(1) == 1 &&
+                    x_scales->size(1) * 128 == x.size(1) && x.stride(0) % 16 == 0 &&
+                    (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0,
+                "fp8 permute: x [N, H] e4m3 (H % 128 == 0, 16-byte aligned rows), scales [N, H/128] fp32, bf16 out");
+    permute_copy_fp8_kernel<<<sms * 4, 256, 0, s>>>(
+        static_cast<const uint8_t*>(x.data_ptr()), x.stride(0), x_scales->data_ptr<float>(), x_scales->stride(0), N, K,
+        static_cast<int>(x.size(1)), pos.data_ptr<int32_t>(), static_cast<__nv_bfloat16*>(out.data_ptr()),
+        offsets.data_ptr<int64_t>(), counts.data_ptr<int32_t>(), EL);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   const int64_t xs = x.stride(0) * x.element_size();
   const uintptr_t xp = reinterpret_cast<uintptr_t>(x.data_ptr()), op = reinterpret_cast<uintptr_t>(out.data_ptr());
   const bool bulk = error.has_value() && ((xp | op) & 15) == 0 && xs % 16 == 0 && row_bytes <= 65536 &&

@@ -94,7 +94,8 @@ void grouped_gemm_k(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
 void router_topk(const at::Tensor& logits, int64_t topk, at::Tensor idx, at::Tensor w);
 void router_topk_bwd(const at::Tensor& idx, const at::Tensor& w, const at::Tensor& dw, at::Tensor dlogits);
 void permute(const at::Tensor& x, const at::Tensor& ids, int64_t num_local_experts, at::Tensor out, at::Tensor pos,
-             at::Tensor offsets, at::Tensor counts, at::Tensor scratch, const OptTensor& error);
+             at::Tensor offsets, at::Tensor counts, at::Tensor scratch, const OptTensor& error,
+             const OptTensor& x_scales);
 void unpermute(const at::Tensor& rows, const at::Tensor& pos, const at::Tensor& w, at::Tensor y);
 void unpermute_bwd(const at::Tensor& dy, const at::Tensor& rows, const at::Tensor& pos, const at::Tensor& w,
                    at::Tensor drows, const OptTensor& dw, const at::Tensor& offsets, const at::Tensor& counts);

@@ -53,7 +53,7 @@ def _expert_forward(rows, offsets, W1, W2):
 
 class _MoEFunction(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, Wr, W1, W2, buf, num_experts, topk, router_bias=None):
+    def forward(ctx, x, Wr, W1, W2, buf, num_experts, topk, router_bias=None, fp8_dispatch=False):
         EL = num_experts // buf.group_size
         with timer.stage('moe.router'):
             logits = router_logits(x, Wr)
@@ -62,9 +62,11 @@ class _MoEFunction(torch.autograd.Function):
             idx, w = MO.router_topk(logits, topk)
         with timer.stage('moe.dispatch'):
             ntr, _, nte, itr, _ = buf.get_dispatch_layout(idx, num_experts)
+            # fp8_dispatch: tokens travel as e4m3 with 1x128 scales (quantised inside the
+            # dispatch kernel) and are dequantised to bf16 by the permute
             recv_x, recv_idx, recv_w, per_expert, handle, _ = buf.dispatch(
                 x, topk_idx=idx, topk_weights=w, num_tokens_per_rank=ntr, is_token_in_rank=itr,
-                num_tokens_per_expert=nte)
+                num_tokens_per_expert=nte, use_fp8=fp8_dispatch)
         with timer.stage('moe.permute'):
             rows, pos, offsets, counts = MO.permute(recv_x, recv_idx, EL, per_expert)
         with timer.stage('moe.experts'):
@@ -109,14 +111,15 @@ class _MoEFunction(torch.autograd.Function):
             else:  # the token-major operand path tiles M in 64-wide atoms
                 dWr = G.grouped_gemm_wgrad(MO.transpose(dlogits), MO.transpose(x), seg, out_dtype=Wr.dtype,
                                            layout='mk')[0]
-        return dx, dWr, dW1, dW2, None, None, None, None
+        return dx, dWr, dW1, dW2, None, None, None, None, None
 
 
 class MoELayer(nn.Module):
     """SwiGLU mixture-of-experts layer with expert parallelism over ``buffer``'s EP group."""
 
     def __init__(self, buffer, hidden: int, intermediate: int, num_experts: int, topk: int,
-                 dtype=torch.bfloat16, device=None, init_std: float = 0.02, seed: int = 0):
+                 dtype=torch.bfloat16, device=None, init_std: float = 0.02, seed: int = 0,
+                 fp8_dispatch: bool = False):
         super().__init__()
         R = buffer.group_size
         if num_experts % R:
@@ -124,6 +127,7 @@ class MoELayer(nn.Module):
         if intermediate % 128 or hidden % 128:
             raise ValueError('hidden and intermediate must be multiples of 128')
         self.buffer = buffer
+        self.fp8_dispatch = fp8_dispatch   # forward tokens cross NVLink as fp8 e4m3 + 1x128 scales
         self.hidden, self.intermediate = hidden, intermediate
         self.num_experts, self.topk = num_experts, topk
         EL = num_experts // R
@@ -147,7 +151,7 @@ class MoELayer(nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return _MoEFunction.apply(x, self.router, self.w1, self.w2, self.buffer, self.num_experts, self.topk,
-                                  self.router_bias)
+                                  self.router_bias, self.fp8_dispatch)
 
 
 def reference_moe(x, Wr, W1, W2, topk, router_bias=None):

@@ -41,13 +41,21 @@ def router_topk_bwd(idx: torch.Tensor, w: torch.Tensor, dw: torch.Tensor, num_ex
     return out
 
 
-def permute(x: torch.Tensor, local_ids: torch.Tensor, num_local_experts: int, counts: list[int] | None = None):
+def permute(x, local_ids: torch.Tensor, num_local_experts: int, counts: list[int] | None = None):
     """Rows of ``x`` [N, H] grouped by local expert, each segment padded to a multiple of 128.
 
+    ``x`` may also be an fp8 pair ``(x_e4m3 [N, H], scales [N, H/128] fp32)`` (what an fp8
+    dispatch delivers); the rows are then dequantised to bf16 on the way.
     Returns ``(rows [P, H], pos [N, K] int32, offsets [EL+1] int64, counts [EL] int32)``;
     ``pos[n, k]`` is the row of pair (n, k) or -1. ``counts`` (host list), when known,
     sizes ``rows`` exactly without a device synchronisation.
     """
+    scales = None
+    if isinstance(x, tuple):
+        x, scales = x
+        if not x.is_cuda:
+            from ..utils.codec import dequantize_fp8_1x128
+            x, scales = dequantize_fp8_1x128(x, scales).to(torch.bfloat16), None
     N, H = x.shape
     K = local_ids.shape[1]
     EL = num_local_experts
@@ -68,14 +76,16 @@ def permute(x: torch.Tensor, local_ids: torch.Tensor, num_local_experts: int, co
                     fill[e] += 1
         return rows, pos, torch.tensor(offs, dtype=torch.int64), torch.tensor(counts, dtype=torch.int32)
     dev = x.device
-    rows = torch.empty(offs[-1], H, dtype=x.dtype, device=dev)
+    rows = torch.empty(offs[-1], H, dtype=torch.bfloat16 if scales is not None else x.dtype, device=dev)
     pos = torch.empty(N, K, dtype=torch.int32, device=dev)
     offsets = torch.empty(EL + 1, dtype=torch.int64, device=dev)
     cnt = torch.empty(EL, dtype=torch.int32, device=dev)
     nblocks = max(1, (N + 31) // 32)
     scratch = torch.empty(nblocks * EL, dtype=torch.int32, device=dev)
     from .gemm import _err  # the kernels' shared device error word (timed-out copies)
-    load().permute(x, local_ids.contiguous(), EL, rows, pos, offsets, cnt, scratch, _err(dev))
+    xq = x.view(torch.uint8) if scales is not None else x
+    load().permute(xq, local_ids.contiguous(), EL, rows, pos, offsets, cnt, scratch, _err(dev),
+                   scales.float().contiguous() if scales is not None else None)
     return rows, pos, offsets, cnt
 
 
