@@ -82,6 +82,16 @@ def main():
     dW2f = torch.empty(E, H, I, device=dev, dtype=torch.float32)
     ms = timed(lambda: G.grouped_gemm_wgrad(dOt, ht, offs, out=dW2f, layout='mk'), args.iters, flush)
     res['wgrad2_mk_f32'] = dict(ms=round(ms, 4), tflops=round(f2 / ms / 1e9, 1))
+    # fp8 block-scaled (e4m3, power-of-two 1x128 scales), same shapes
+    qa, sa = G.quantize_fp8_blocks(A)
+    qw1, sw1 = G.quantize_fp8_blocks(W1)
+    qh, shh = G.quantize_fp8_blocks(h)
+    qw2, sw2 = G.quantize_fp8_blocks(W2)
+    ms = timed(lambda: G.grouped_gemm_fp8(qa, sa, qw1, sw1, offs, out=pre, epilogue='swiglu', h_out=h), args.iters,
+               flush)
+    res['fp8_gemm1_swiglu'] = dict(ms=round(ms, 4), tflops=round(f1 / ms / 1e9, 1))
+    ms = timed(lambda: G.grouped_gemm_fp8(qh, shh, qw2, sw2, offs, out=out), args.iters, flush)
+    res['fp8_gemm2'] = dict(ms=round(ms, 4), tflops=round(f2 / ms / 1e9, 1))
     G.check()
     if not args.no_cublas:
         def cublas1():

@@ -55,6 +55,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("transpose", &transpose);
   m.def("grouped_gemm_k", &grouped_gemm_k);
+  m.def("grouped_gemm_fp8_m", &grouped_gemm_fp8_m);
   m.def("wait_probe", &wait_probe);
   m.def("fence_cost", &fence_cost);
 }

@@ -58,6 +58,11 @@ struct Args {
   int64_t ldr;
   uint32_t* error;          // device word, non-zero after a timeout
   uint64_t timeout_ns;
+  // fp8 block-scaled mode: one power-of-two fp32 scale per (row, 128-channel K block)
+  const float* sfa;         // [rows of A, ceil(K / 128)], row stride sfa_ld
+  int64_t sfa_ld;
+  const float* sfb;         // [G * N, ceil(K / 128)], row stride sfb_ld
+  int64_t sfb_ld;
 };
 
 // ----------------------------------------------------------------------------- PTX wrappers
@@ -106,6 +111,22 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+// D (+)= (A * SFA) x (B * SFB)^T for e4m3 operands, K = 32 per instruction, with one UE8M0
+// scale per 32 K-elements of each row of A and of B read from tensor memory.
+__device__ __forceinline__ void tc_mma_fp8_bs(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate, uint32_t tmem_sfa, uint32_t tmem_sfb) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tmem_sfa), "r"(tmem_sfb)
+      : "memory");
+}
+// 32 rows x 16 bytes of shared memory -> 32 TMEM lanes x 4 columns, written to all four
+// 32-lane subpartitions (the replicated layout the block-scaled MMA reads scales from).
+__device__ __forceinline__ void tc_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 __device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
@@ -160,6 +181,33 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int n, bool a_mn = false, bool
 }
 constexpr uint32_t kMnAtomBytes = 64 * BK * 2;  // one 64-wide MN column of a BK-deep stage
 
+// Instruction descriptor of the block-scaled fp8 MMA: A/B e4m3, K-major, UE8M0 scales,
+// scale byte 0 of each TMEM word for both operands, M=128, N=n, K=32.
+__host__ __device__ constexpr uint32_t idesc_fp8_bs(int n) {
+  return (0u << 4) | (0u << 7) | (0u << 10) | (uint32_t(n >> 3) << 17) | (1u << 23) | (uint32_t(BM >> 4) << 24);
+}
+// Shared-memory descriptor of a dense, unswizzled 32-row x 16-byte tile (the source of
+// tcgen05.cp 32x128b): rows 16 bytes apart, 8-row core matrices 128 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sf(const void* p) {
+  const uint64_t addr = smem_u32(p);
+  uint64_t d = (addr >> 4) & 0x3FFFull;
+  d |= (128ull >> 4) << 16;   // leading byte offset (a single core matrix along K: unused)
+  d |= (128ull >> 4) << 32;   // stride byte offset: next 8 rows
+  d |= 1ull << 46;            // descriptor version for sm_100; layout type 0 = no swizzle
+  return d;
+}
+// fp8 mode: K elements per pipeline stage (128 one-byte elements fill the 128-byte swizzle row)
+constexpr int BK8 = 128;
+// Scale-factor staging per stage: SFA (128 rows) then SFB (BN rows), 16 bytes per 4 rows.
+template <int BN>
+__host__ __device__ constexpr int sf_stage_bytes() { return (BM + BN) * 4; }
+// UE8M0 byte of a power-of-two fp32 scale (its biased exponent), copied into all four
+// bytes of a word so every scale slot of the TMEM word holds it.
+__device__ __forceinline__ uint32_t ue8m0_word(float s) {
+  const uint32_t e = (__float_as_uint(s) >> 23) & 0xFFu;
+  return e * 0x01010101u;
+}
+
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const Args& a) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
@@ -210,7 +258,7 @@ struct Tile {
   int kb0, nkb;  // k-block range
 };
 
-template <bool GROUP_K, int BN>
+template <bool GROUP_K, int BN, int KBLK = BK>
 __device__ __forceinline__ bool tile_of(int t, const Args& a, const int64_t* offs, Tile& tl) {
   const int ntiles_n = (a.N + BN - 1) / BN;
   if (!GROUP_K) {
@@ -228,7 +276,7 @@ __device__ __forceinline__ bool tile_of(int t, const Args& a, const int64_t* off
     }
     tl.g = lo;
     tl.kb0 = 0;
-    tl.nkb = (a.K + BK - 1) / BK;
+    tl.nkb = (a.K + KBLK - 1) / KBLK;
   } else {
     const int ntiles_m = (a.M + BM - 1) / BM;
     const int per = ntiles_m * ntiles_n;
@@ -245,7 +293,9 @@ __device__ __forceinline__ bool tile_of(int t, const Args& a, const int64_t* off
 
 // LAYOUT bit 0: A is MN-major; bit 1: B is MN-major (GROUP_M: B is [G, K, N], read
 // through a 3-D map so a K tail never reaches into the next expert's weight).
-template <bool GROUP_K, int BN, int STAGES, int EPI, int LAYOUT>
+// FP8: A and B are e4m3 (K-major, GROUP_M only) with power-of-two fp32 scales per
+// (row, 128-channel block); the MMA applies them (kind::mxf8f6f4.block_scale).
+template <bool GROUP_K, int BN, int STAGES, int EPI, int LAYOUT, bool FP8 = false>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmH, Args a) {
@@ -256,7 +306,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::kABytes;
   uint8_t* sE = sB + STAGES * S::kBBytes;  // epilogue staging, kEpiWarpBytes per epilogue warp
-  uint64_t* full = reinterpret_cast<uint64_t*>(sE + kEpiBytes);
+  uint8_t* sSF = sE + kEpiBytes;           // fp8 mode: per-stage scale tiles
+  constexpr int kSF = FP8 ? sf_stage_bytes<BN>() : 0;
+  constexpr int KBLK = FP8 ? BK8 : BK;     // K elements per stage
+  static_assert(!FP8 || (!GROUP_K && LAYOUT == 0 && BN <= 128), "fp8: grouped-M, K-major, N tile <= 128");
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSF + STAGES * kSF);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -290,7 +344,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
+  if (FP8 && warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (fp8)
+    // lane 0 waits and issues the tile loads; all lanes write the stage's scale tiles
+    uint32_t it = 0;
+    Tile tl;
+    bool go = true;
+    for (int t = blockIdx.x; go && tile_of<GROUP_K, BN, KBLK>(t, a, s_offs, tl); t += gridDim.x) {
+      for (int kb = 0; kb < tl.nkb; ++kb, ++it) {
+        const int s = it % STAGES;
+        int ok = 1;
+        if (lane == 0) ok = !s_abort && wait_bar(&empty[s], ((it / STAGES) & 1u) ^ 1u, a);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+          if (lane == 0) s_abort = 1;
+          go = false;
+          break;
+        }
+        const int kg = tl.kb0 + kb;  // 128-channel block index
+        uint32_t* sf = reinterpret_cast<uint32_t*>(sSF + s * kSF);
+        // row r's word sits at 16 * (r % 32) + 4 * (r / 32) bytes: TMEM lane r % 32, column r / 32
+#pragma unroll
+        for (int j = 0; j < BM / 32; ++j) {
+          const int r = lane + 32 * j;
+          const int64_t row = static_cast<int64_t>(tl.m0) + r;
+          const float v = row < a.M ? a.sfa[row * a.sfa_ld + kg] : 1.f;
+          sf[lane * 4 + j] = ue8m0_word(v);
+        }
+#pragma unroll
+        for (int j = 0; j < BN / 32; ++j) {
+          const int r = lane + 32 * j;
+          const int n = tl.n0 + r;
+          const float v = n < a.N ? a.sfb[(static_cast<int64_t>(tl.g) * a.N + n) * a.sfb_ld + kg] : 1.f;
+          sf[BM + (j / 4) * 128 + lane * 4 + (j % 4)] = ue8m0_word(v);
+        }
+        fence_proxy_async_smem();  // the scale tiles are read by tcgen05.cp (async proxy)
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+          const int kc = kg * KBLK;
+          tma_load_2d(sA + s * S::kABytes, &tmA, &full[s], kc, tl.m0);
+          tma_load_2d(sB + s * S::kBBytes, &tmB, &full[s], kc, tl.g * a.N + tl.n0);
+        }
+      }
+    }
+  } else if (!FP8 && warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       uint32_t it = 0;
@@ -321,6 +419,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+  } else if (FP8 && warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (fp8, block-scaled)
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_fp8_bs(BN);
+      constexpr uint32_t kSfCol0 = 2 * BN;   // scale columns follow the two accumulators
+      uint32_t it = 0, acc = 0;
+      Tile tl;
+      for (int t = blockIdx.x; tile_of<GROUP_K, BN, KBLK>(t, a, s_offs, tl) && !s_abort; t += gridDim.x) {
+        if (tl.nkb == 0) continue;
+        const int b = acc & 1;
+        if (!wait_bar(&tempty[b], ((acc >> 1) & 1u) ^ 1u, a)) { s_abort = 1; break; }
+        tc_fence_after();
+        const uint32_t dcol = tmem_base + b * BN;
+        bool ok = true;
+        for (int kb = 0; kb < tl.nkb; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!wait_bar(&full[s], (it / STAGES) & 1u, a)) { ok = false; break; }
+          tc_fence_after();
+          // this stage's scales: SFA in 4 columns, SFB in BN / 32 columns
+          const uint32_t sfa_t = tmem_base + kSfCol0 + s * (4 + BN / 32);
+          const uint32_t sfb_t = sfa_t + 4;
+          const uint8_t* sf = sSF + s * kSF;
+          tc_cp_32x128b_x4(sfa_t, smem_desc_sf(sf));
+#pragma unroll
+          for (int j = 0; j < BN / 128; ++j) tc_cp_32x128b_x4(sfb_t + 4 * j, smem_desc_sf(sf + 512 + 512 * j));
+          const uint64_t ad = smem_desc_k128(sA + s * S::kABytes);
+          const uint64_t bd = smem_desc_k128(sB + s * S::kBBytes);
+          // 4 MMAs of K = 32 one-byte elements: 32 bytes (2 units) along the swizzle row each
+#pragma unroll
+          for (int k = 0; k < BK8 / 32; ++k)
+            tc_mma_fp8_bs(dcol, ad + 2 * k, bd + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u, sfa_t, sfb_t);
+          tc_commit(&empty[s]);
+        }
+        if (!ok) { s_abort = 1; break; }
+        tc_commit(&tfull[b]);
+        ++acc;
+      }
+      tc_commit(drain);
+      wait_bar(drain, 0, a);
+    }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -332,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int b = acc & 1;
         if (!wait_bar(&tempty[b], ((acc >> 1) & 1u) ^ 1u, a)) { s_abort = 1; break; }
         tc_fence_after();
-        const uint32_t dcol = tmem_base + b * 256;
+        const uint32_t dcol = tmem_base + b * BN;
         bool ok = true;
         for (int kb = 0; kb < tl.nkb; ++kb, ++it) {
           const int s = it % STAGES;
@@ -382,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     uint32_t acc = 0;
     Tile tl;
-    for (int t = blockIdx.x; tile_of<GROUP_K, BN>(t, a, s_offs, tl); t += gridDim.x) {
+    for (int t = blockIdx.x; tile_of<GROUP_K, BN, KBLK>(t, a, s_offs, tl); t += gridDim.x) {
       const int b = acc & 1;
       const bool have = tl.nkb > 0;
       if (have) {
@@ -390,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (s_abort) break;
         tc_fence_after();
       }
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * 256;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + b * BN;
       const int row0 = tl.m0 + q * 32;         // first row of this warp's boxes
       // boxes that start past the output are skipped; the map clips partial ones
       const bool rows_in = GROUP_K ? row0 < a.M : row0 < a.c_rows;
@@ -544,11 +682,28 @@ CUtensorMap make_out_map(void* base, bool f32, int64_t rows, int64_t cols, int64
   return m;
 }
 
-template <bool GROUP_K, int BN, int STAGES, int EPI, int LAYOUT>
+// 2-D one-byte [rows, cols] (row stride ld bytes), boxes of box_rows x 128 bytes, 128B swizzle.
+CUtensorMap make_map_u8(const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK(ld % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK8), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (u8) failed: ", static_cast<int>(r));
+  return m;
+}
+
+template <bool GROUP_K, int BN, int STAGES, int EPI, int LAYOUT, bool FP8 = false>
 void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mh,
             const Args& a, int grid, cudaStream_t stream) {
-  constexpr size_t smem = 1024 + STAGES * Smem<BN>::kStageBytes + kEpiBytes + (2 * STAGES + 5) * 8 + 16;
-  auto kfn = grouped_gemm_kernel<GROUP_K, BN, STAGES, EPI, LAYOUT>;
+  constexpr size_t smem = 1024 + STAGES * Smem<BN>::kStageBytes + kEpiBytes +
+                          (FP8 ? STAGES * sf_stage_bytes<BN>() : 0) + (2 * STAGES + 5) * 8 + 16;
+  auto kfn = grouped_gemm_kernel<GROUP_K, BN, STAGES, EPI, LAYOUT, FP8>;
   static bool set = false;
   if (!set) {
     AT_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
@@ -667,6 +822,67 @@ void grouped_gemm_k(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
     if (f32) launch<true, 256, 4, kEpiF32, 0>(ma, mb, mc, mc, a, sms, stream);
     else launch<true, 256, 4, kEpiBF16, 0>(ma, mb, mc, mc, a, sms, stream);
   }
+}
+
+// fp8 block-scaled grouped GEMM (forward shape): C[seg_g] = dequant(A)[seg_g] @ dequant(B[g])^T with
+// A [rows, K] e4m3 and B [G, N, K] e4m3, each with one power-of-two fp32 scale per (row,
+// 128-channel K block): sa [rows, K/128], sb [G, N, K/128]. Scales must be exact powers of two
+// (the tensor cores take them as UE8M0 exponents). Epilogues as grouped_gemm_m; the SwiGLU
+// epilogue expects 64-row gate / up blocks (N tiles of 128).
+void grouped_gemm_fp8_m(const at::Tensor& A, const at::Tensor& sa, const at::Tensor& B, const at::Tensor& sb,
+                        const at::Tensor& offsets, const OptTensor& C, const OptTensor& Hout, int64_t epilogue,
+                        at::Tensor error, int64_t num_sms, double timeout_s) {
+  using namespace gemm;
+  const c10::cuda::CUDAGuard guard(A.device());
+  TORCH_CHECK(A.element_size() == 1 && B.element_size() == 1, "A, B must be one-byte (e4m3) tensors");
+  TORCH_CHECK(A.dim() == 2 && A.stride(1) == 1 && B.dim() == 3 && B.is_contiguous(), "A [rows, K], B [G, N, K]");
+  TORCH_CHECK(offsets.scalar_type() == at::kLong && offsets.numel() == B.size(0) + 1 && B.size(0) <= 1024,
+              "offsets must be [G + 1] int64, G <= 1024");
+  Args a{};
+  a.G = static_cast<int>(B.size(0));
+  a.N = static_cast<int>(B.size(1));
+  a.K = static_cast<int>(B.size(2));
+  a.M = static_cast<int>(A.size(0));
+  TORCH_CHECK(A.size(1) == a.K && a.K % 128 == 0, "K mismatch, or K not a multiple of 128");
+  const int64_t KB = a.K / 128;
+  TORCH_CHECK(sa.scalar_type() == at::kFloat && sa.dim() == 2 && sa.size(0) == A.size(0) && sa.size(1) == KB &&
+                  sa.stride(1) == 1,
+              "sa must be [rows, K/128] fp32");
+  TORCH_CHECK(sb.scalar_type() == at::kFloat && sb.is_contiguous() && sb.numel() == int64_t(a.G) * a.N * KB,
+              "sb must be [G, N, K/128] fp32");
+  a.sfa = sa.data_ptr<float>();
+  a.sfa_ld = sa.stride(0);
+  a.sfb = sb.data_ptr<float>();
+  a.sfb_ld = KB;
+  a.offsets = offsets.data_ptr<int64_t>();
+  a.error = reinterpret_cast<uint32_t*>(error.data_ptr<int32_t>());
+  a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);
+  constexpr int BN8 = 128;
+  const CUtensorMap ma = make_map_u8(A.data_ptr(), A.size(0), a.K, A.stride(0), BM);
+  const CUtensorMap mb = make_map_u8(B.data_ptr(), int64_t(a.G) * a.N, a.K, a.K, BN8);
+  a.c_rows = A.size(0);
+  if (epilogue == kEpiSwiGLU) {
+    TORCH_CHECK(a.N % BN8 == 0 && Hout.has_value(), "SwiGLU needs N % 128 == 0 and an H output");
+    a.H = Hout->data_ptr();
+    a.ldh = Hout->stride(0);
+    TORCH_CHECK(Hout->size(0) >= A.size(0), "H needs as many rows as A");
+  }
+  if (C.has_value()) {
+    TORCH_CHECK(C->size(0) >= A.size(0) && C->stride(1) == 1, "C needs at least as many rows as A");
+    TORCH_CHECK((epilogue == kEpiF32) == (C->scalar_type() == at::kFloat), "C dtype does not match the epilogue");
+    a.C = C->data_ptr();
+    a.ldc = C->stride(0);
+  } else {
+    TORCH_CHECK(epilogue == kEpiSwiGLU, "C is required");
+  }
+  const CUtensorMap mh = epilogue == kEpiSwiGLU ? make_out_map(a.H, false, a.c_rows, a.N / 2, a.ldh, 0)
+                                                : CUtensorMap{};
+  const CUtensorMap mc = a.C ? make_out_map(a.C, epilogue == kEpiF32, a.c_rows, a.N, a.ldc, 0) : mh;
+  const int sms = num_sms > 0 ? static_cast<int>(num_sms) : at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (epilogue == kEpiBF16) launch<false, BN8, 6, kEpiBF16, 0, true>(ma, mb, mc, mh, a, sms, stream);
+  else if (epilogue == kEpiF32) launch<false, BN8, 6, kEpiF32, 0, true>(ma, mb, mc, mh, a, sms, stream);
+  else launch<false, BN8, 6, kEpiSwiGLU, 0, true>(ma, mb, mc, mh, a, sms, stream);
 }
 
 }  // namespace b200ep

@@ -87,6 +87,9 @@ void fence_cost(SymmHeap& heap, int64_t peer, int64_t bytes, int64_t scope, at::
 void grouped_gemm_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, const OptTensor& C,
                     const OptTensor& Hout, int64_t epilogue, at::Tensor error, int64_t num_sms, double timeout_s,
                     bool b_kn, const OptTensor& residual);
+void grouped_gemm_fp8_m(const at::Tensor& A, const at::Tensor& sa, const at::Tensor& B, const at::Tensor& sb,
+                        const at::Tensor& offsets, const OptTensor& C, const OptTensor& Hout, int64_t epilogue,
+                        at::Tensor error, int64_t num_sms, double timeout_s);
 void grouped_gemm_k(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, at::Tensor C,
                     at::Tensor error, int64_t num_sms, double timeout_s, bool tok_major);
 

@@ -3,6 +3,7 @@
 ``grouped_gemm``       C[seg_e] = A[seg_e] @ B[e]^T      A [rows, K], B [G, N, K]   (forward)
                        C[seg_e] = A[seg_e] @ B[e]        A [rows, K], B [G, K, N]   (``b_layout='kn'``: dX)
 ``grouped_gemm_wgrad`` C[e] = A[seg_e]^T @ B[seg_e]      A [tok, M], B [tok, N]     (dW)
+``grouped_gemm_fp8``   C[seg_e] = A[seg_e] @ B[e]^T      e4m3 A, B with 1x128 power-of-two scales
                        C[e] = A[:, seg_e] @ B[:, seg_e]^T A [M, tok], B [N, tok]    (``layout='mk'``)
 
 Transposed operands are read in place by the tensor cores (MN-major shared-memory
@@ -70,6 +71,38 @@ def grouped_gemm_wgrad(A: torch.Tensor, B: torch.Tensor, offsets: torch.Tensor, 
     M, N = (A.shape[1], B.shape[1]) if tok else (A.shape[0], B.shape[0])
     c = out if out is not None else torch.empty(G, M, N, dtype=out_dtype, device=A.device)
     load().grouped_gemm_k(A, B, offsets, c, _err(A.device), num_sms, timeout_s, tok)
+    return c
+
+
+def quantize_fp8_blocks(w: torch.Tensor):
+    """e4m3 copy of ``w`` [.., K] with one power-of-two fp32 scale per (row, 128-channel block):
+    the operand format of ``grouped_gemm_fp8`` (the tensor cores apply the scales as UE8M0
+    exponents, so they must be powers of two)."""
+    from ..utils.codec import quantize_fp8_1x128
+    q, sc = quantize_fp8_1x128(w, round_scale=True)
+    return q.contiguous(), sc.contiguous()
+
+
+def grouped_gemm_fp8(A, sa, B, sb, offsets, out=None, epilogue: str = 'bf16', h_out=None, save_preact: bool = True,
+                     num_sms: int = 0, timeout_s: float = 10.0):
+    """Block-scaled fp8 grouped GEMM on the tensor cores (``tcgen05.mma ... kind::mxf8f6f4.block_scale``):
+    ``C[seg_e] = (A * sa)[seg_e] @ (B[e] * sb[e])^T`` with A [rows, K] and B [G, N, K] e4m3, and
+    power-of-two fp32 scales sa [rows, K/128], sb [G, N, K/128] (``quantize_fp8_blocks``).
+    fp32 accumulation; epilogues as ``grouped_gemm``. The SwiGLU epilogue reads each 128-wide
+    output tile as [64 gate | 64 up] (``interleave_gate_up(..., block=64)``)."""
+    rows, N = A.shape[0], B.shape[1]
+    a8, b8 = A.view(torch.uint8), B.view(torch.uint8)
+    sa, sb = sa.float(), sb.float().contiguous()
+    if epilogue == 'swiglu':
+        h = h_out if h_out is not None else torch.empty(rows, N // 2, dtype=torch.bfloat16, device=A.device)
+        c = (out if out is not None else torch.empty(rows, N, dtype=torch.bfloat16, device=A.device)) \
+            if save_preact else None
+        load().grouped_gemm_fp8_m(a8, sa, b8, sb, offsets, c, h, 2, _err(A.device), num_sms, timeout_s)
+        return h, c
+    dtype = torch.float32 if epilogue == 'f32' else torch.bfloat16
+    c = out if out is not None else torch.empty(rows, N, dtype=dtype, device=A.device)
+    load().grouped_gemm_fp8_m(a8, sa, b8, sb, offsets, c, None, EPILOGUES[epilogue], _err(A.device), num_sms,
+                              timeout_s)
     return c
 
 

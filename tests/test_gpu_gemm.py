@@ -131,3 +131,64 @@ def test_grouped_gemm_residual_epilogue():
     torch.cuda.synchronize()
     check()
     _close(C, A.float() @ B[0].float() + R.float(), tol=1e-2)
+
+
+def _fp8_operand(shape, g, row_spread=True):
+    """Random data whose rows and 128-channel blocks differ in magnitude (so that every
+    scale differs), quantised to e4m3 with power-of-two 1x128 scales."""
+    from deepep_trn_b200.ops.gemm import quantize_fp8_blocks
+    x = torch.randn(*shape, generator=g)
+    K = shape[-1]
+    blk = torch.pow(2.0, torch.randint(-3, 4, (*shape[:-1], K // 128), generator=g).float())
+    x = x * blk.repeat_interleave(128, -1)
+    q, sc = quantize_fp8_blocks(x.cuda())
+    deq = (q.float().reshape(*shape[:-1], K // 128, 128) * sc.unsqueeze(-1)).reshape(shape)
+    return q, sc, deq
+
+
+@needs_cuda
+@pytest.mark.parametrize('counts,N,K', [([128, 0, 256], 128, 256), ([100, 300], 384, 640),
+                                        ([1024, 896, 128, 1280], 2048, 7168)])
+def test_grouped_gemm_fp8_block_scaled(counts, N, K):
+    from deepep_trn_b200.ops.gemm import check, grouped_gemm_fp8
+    g = torch.Generator().manual_seed(11)
+    G = len(counts)
+    offs = _segments(counts)
+    qa, sa, A = _fp8_operand((offs[-1], K), g)
+    qb, sb, B = _fp8_operand((G, N, K), g)
+    o = torch.tensor(offs, dtype=torch.int64, device='cuda')
+    C = grouped_gemm_fp8(qa, sa, qb, sb, o)
+    Cf = grouped_gemm_fp8(qa, sa, qb, sb, o, epilogue='f32')
+    torch.cuda.synchronize()
+    check()
+    for e in range(G):
+        s, t = offs[e], offs[e] + counts[e]
+        ref = A[s:t] @ B[e].t()      # fp32 product of the same quantised operands
+        _close(Cf[s:t], ref, tol=1e-3)
+        _close(C[s:t], ref)
+
+
+@needs_cuda
+def test_grouped_gemm_fp8_swiglu():
+    from deepep_trn_b200.ops.gemm import check, deinterleave, grouped_gemm_fp8, interleave_gate_up
+    g = torch.Generator().manual_seed(12)
+    counts, I, K = [256, 384], 256, 1024
+    G = len(counts)
+    offs = _segments(counts)
+    qa, sa, A = _fp8_operand((offs[-1], K), g)
+    qg, sg, Wg = _fp8_operand((G, I, K), g)
+    qu, su, Wu = _fp8_operand((G, I, K), g)
+    qw = interleave_gate_up(qg.view(torch.uint8), qu.view(torch.uint8), block=64).view(torch.float8_e4m3fn)
+    sw = interleave_gate_up(sg, su, block=64)
+    h, pre = grouped_gemm_fp8(qa, sa, qw.contiguous(), sw.contiguous(), torch.tensor(offs, device='cuda'),
+                              epilogue='swiglu')
+    torch.cuda.synchronize()
+    check()
+    for e in range(G):
+        s, t = offs[e], offs[e] + counts[e]
+        gt = A[s:t] @ Wg[e].t()
+        ut = A[s:t] @ Wu[e].t()
+        _close(h[s:t], torch.nn.functional.silu(gt) * ut, tol=3e-2)
+        pg, pu = deinterleave(pre[s:t], block=64)
+        _close(pg, gt)
+        _close(pu, ut)
