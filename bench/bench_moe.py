@@ -35,7 +35,9 @@ def main():
     p.add_argument('--warmup', type=int, default=3)
     p.add_argument('--impls', default='ours,nccl')
     p.add_argument('--breakdown', action='store_true', help='per-phase device time of the fused layer')
-    p.add_argument('--fp8', action='store_true', help='fused layer: forward dispatch in fp8 e4m3 + 1x128 scales')
+    p.add_argument('--fp8', action='store_true', help='fused layer: forward dispatch in fp8 e4m3 + 1x128 scales '
+                   '(with --forward-only also fp8 block-scaled expert GEMMs)')
+    p.add_argument('--forward-only', action='store_true', help='inference: forward under torch.no_grad()')
     p.set_defaults(tokens=[4096])
     args = p.parse_args()
     T = args.tokens[0]
@@ -50,7 +52,8 @@ def main():
     for impl in args.impls.split(','):
         buf = Buffer(ctx.ep_group, backend='nvlink' if impl == 'ours' else 'nccl', num_max_tokens_per_rank=T,
                      hidden=H, num_experts=E, topk=K)
-        layer = (MoELayer(buf, H, I, E, K, device=dev, init_std=0.02, seed=7, fp8_dispatch=args.fp8) if impl == 'ours'
+        layer = (MoELayer(buf, H, I, E, K, device=dev, init_std=0.02, seed=7, fp8_dispatch=args.fp8,
+                          fp8_experts=args.fp8 and args.forward_only) if impl == 'ours'
                  else BaselineMoELayer(buf, H, I, E, K, device=dev))
         with torch.no_grad():
             if params is None:
@@ -71,6 +74,9 @@ def main():
         dy = torch.randn(T, H, generator=torch.Generator().manual_seed(200 + ctx.rank)).to(torch.bfloat16).to(dev)
 
         def step():
+            if args.forward_only:
+                with torch.no_grad():
+                    return layer(x)
             x.grad = None
             for prm in layer.parameters():
                 prm.grad = None
@@ -87,7 +93,8 @@ def main():
             timer.run(step)
         ms = max_over_ranks(timer.total_ms()) / args.steps
         per_step = [round(st.elapsed_time(en), 3) for st, en in timer.events]
-        flops = 18.0 * T * K * H * I  # expert GEMMs per rank on average: forward 6*P*H*I, backward twice that
+        # expert GEMMs per rank on average: forward 6*P*H*I, backward twice that
+        flops = (6.0 if args.forward_only else 18.0) * T * K * H * I
         results[impl] = dict(ms_per_step=round(ms, 3), tokens_per_s=round(T * ctx.ep / (ms * 1e-3), 1),
                              expert_tflops_per_rank=round(flops / (ms * 1e-3) / 1e12, 1), steps_ms_rank0=per_step)
         if args.breakdown and impl == 'ours':
@@ -105,7 +112,9 @@ def main():
         del layer
         torch.cuda.empty_cache()
     rec = dict(bench='moe', ep=ctx.ep, tokens=T, hidden=H, inter=I, experts=E, topk=K, routing='zipf',
-               dispatch_dtype='fp8-e4m3-1x128' if args.fp8 else 'bf16', **results)
+               dispatch_dtype='fp8-e4m3-1x128' if args.fp8 else 'bf16',
+               expert_gemm_dtype='fp8-e4m3-1x128-block-scaled' if (args.fp8 and args.forward_only) else 'bf16',
+               pass_='forward' if args.forward_only else 'forward+backward', **results)
     if 'ours' in results and 'nccl' in results:
         rec['speedup_vs_nccl_cublas'] = round(results['nccl']['ms_per_step'] / results['ours']['ms_per_step'], 3)
     if ctx.rank == 0:

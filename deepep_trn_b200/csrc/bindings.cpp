@@ -56,6 +56,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("transpose", &transpose);
   m.def("grouped_gemm_k", &grouped_gemm_k);
   m.def("grouped_gemm_fp8_m", &grouped_gemm_fp8_m);
+  m.def("sf_tiles", &sf_tiles);
   m.def("wait_probe", &wait_probe);
   m.def("fence_cost", &fence_cost);
 }

@@ -58,11 +58,10 @@ struct Args {
   int64_t ldr;
   uint32_t* error;          // device word, non-zero after a timeout
   uint64_t timeout_ns;
-  // fp8 block-scaled mode: one power-of-two fp32 scale per (row, 128-channel K block)
-  const float* sfa;         // [rows of A, ceil(K / 128)], row stride sfa_ld
-  int64_t sfa_ld;
-  const float* sfb;         // [G * N, ceil(K / 128)], row stride sfb_ld
-  int64_t sfb_ld;
+  // fp8 block-scaled mode: scales as 512-byte tiles, one per (128 rows, 128-channel K block),
+  // already in the layout tcgen05.cp moves to tensor memory (see sf_tiles_kernel)
+  const uint8_t* sfa_tiles; // [ceil(rows / 128), K / 128, 512 B]
+  const uint8_t* sfb_tiles; // [G, ceil(N / 128), K / 128, 512 B]
 };
 
 // ----------------------------------------------------------------------------- PTX wrappers
@@ -201,12 +200,6 @@ constexpr int BK8 = 128;
 // Scale-factor staging per stage: SFA (128 rows) then SFB (BN rows), 16 bytes per 4 rows.
 template <int BN>
 __host__ __device__ constexpr int sf_stage_bytes() { return (BM + BN) * 4; }
-// UE8M0 byte of a power-of-two fp32 scale (its biased exponent), copied into all four
-// bytes of a word so every scale slot of the TMEM word holds it.
-__device__ __forceinline__ uint32_t ue8m0_word(float s) {
-  const uint32_t e = (__float_as_uint(s) >> 23) & 0xFFu;
-  return e * 0x01010101u;
-}
 
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const Args& a) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -346,45 +339,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (FP8 && warp == 0) {
     // ------------------------------------------------------------------ TMA producer (fp8)
-    // lane 0 waits and issues the tile loads; all lanes write the stage's scale tiles
-    uint32_t it = 0;
-    Tile tl;
-    bool go = true;
-    for (int t = blockIdx.x; go && tile_of<GROUP_K, BN, KBLK>(t, a, s_offs, tl); t += gridDim.x) {
-      for (int kb = 0; kb < tl.nkb; ++kb, ++it) {
-        const int s = it % STAGES;
-        int ok = 1;
-        if (lane == 0) ok = !s_abort && wait_bar(&empty[s], ((it / STAGES) & 1u) ^ 1u, a);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) {
-          if (lane == 0) s_abort = 1;
-          go = false;
-          break;
-        }
-        const int kg = tl.kb0 + kb;  // 128-channel block index
-        uint32_t* sf = reinterpret_cast<uint32_t*>(sSF + s * kSF);
-        // row r's word sits at 16 * (r % 32) + 4 * (r / 32) bytes: TMEM lane r % 32, column r / 32
-#pragma unroll
-        for (int j = 0; j < BM / 32; ++j) {
-          const int r = lane + 32 * j;
-          const int64_t row = static_cast<int64_t>(tl.m0) + r;
-          const float v = row < a.M ? a.sfa[row * a.sfa_ld + kg] : 1.f;
-          sf[lane * 4 + j] = ue8m0_word(v);
-        }
-#pragma unroll
-        for (int j = 0; j < BN / 32; ++j) {
-          const int r = lane + 32 * j;
-          const int n = tl.n0 + r;
-          const float v = n < a.N ? a.sfb[(static_cast<int64_t>(tl.g) * a.N + n) * a.sfb_ld + kg] : 1.f;
-          sf[BM + (j / 4) * 128 + lane * 4 + (j % 4)] = ue8m0_word(v);
-        }
-        fence_proxy_async_smem();  // the scale tiles are read by tcgen05.cp (async proxy)
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+    // per stage: the A and B tiles plus their two 512-byte scale tiles (bulk copies)
+    if (lane == 0) {
+      uint32_t it = 0;
+      Tile tl;
+      const int KB = (a.K + KBLK - 1) / KBLK;
+      const int ntn = (a.N + BN - 1) / BN;
+      for (int t = blockIdx.x; tile_of<GROUP_K, BN, KBLK>(t, a, s_offs, tl) && !s_abort; t += gridDim.x) {
+        for (int kb = 0; kb < tl.nkb; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!wait_bar(&empty[s], ((it / STAGES) & 1u) ^ 1u, a)) { s_abort = 1; break; }
+          mbar_arrive_expect_tx(&full[s], S::kStageBytes + kSF);
+          const int kg = tl.kb0 + kb;
           const int kc = kg * KBLK;
           tma_load_2d(sA + s * S::kABytes, &tmA, &full[s], kc, tl.m0);
           tma_load_2d(sB + s * S::kBBytes, &tmB, &full[s], kc, tl.g * a.N + tl.n0);
+          uint8_t* sf = sSF + s * kSF;
+          bulk_load(sf, a.sfa_tiles + (static_cast<int64_t>(tl.m0 / BM) * KB + kg) * 512, 512, &full[s]);
+          bulk_load(sf + 512,
+                    a.sfb_tiles + ((static_cast<int64_t>(tl.g) * ntn + tl.n0 / BN) * KB + kg) * 512, 512, &full[s]);
         }
       }
     }
@@ -824,6 +797,42 @@ void grouped_gemm_k(const at::Tensor& A, const at::Tensor& B, const at::Tensor& 
   }
 }
 
+// Scale tiles for the fp8 GEMM: scales [groups * rows, KB] fp32 (powers of two) ->
+// [groups, ceil(rows / 128), KB] tiles of 128 words; word (r % 32) * 4 + r / 32 holds row r's
+// UE8M0 exponent in all four bytes (after a 32x128b copy: TMEM lane r % 32 of every
+// subpartition, column r / 32). Rows past a group's `rows` read as scale 1.
+__global__ void sf_tiles_kernel(const float* __restrict__ sc, int64_t ld, int64_t rows, int64_t tiles, int KB,
+                                uint32_t* __restrict__ out, int64_t total) {
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int w = static_cast<int>(i & 127);
+    const int64_t tk = i >> 7;          // (group, row tile, kb)
+    const int kb = static_cast<int>(tk % KB);
+    const int64_t gt = tk / KB;
+    const int64_t tile = gt % tiles, g = gt / tiles;
+    const int64_t r = tile * 128 + (w >> 2) + 32 * (w & 3);
+    const float v = r < rows ? sc[(g * rows + r) * ld + kb] : 1.f;
+    out[i] = ((__float_as_uint(v) >> 23) & 0xFFu) * 0x01010101u;
+  }
+}
+
+at::Tensor sf_tiles(const at::Tensor& sc, int64_t groups, int64_t rows_per_group) {
+  // sc: [groups * rows_per_group, KB] fp32 -> uint8 [groups, ceil(rows_per_group / 128), KB, 512]
+  TORCH_CHECK(sc.scalar_type() == at::kFloat && sc.dim() == 2 && sc.stride(1) == 1 &&
+                  sc.size(0) == groups * rows_per_group,
+              "scales must be [groups * rows, KB] fp32");
+  const int KB = static_cast<int>(sc.size(1));
+  const int64_t tiles = (rows_per_group + 127) / 128;
+  auto out = at::empty({groups, tiles, KB, 512}, sc.options().dtype(at::kByte));
+  const int64_t total = groups * tiles * KB * 128;
+  if (total == 0) return out;
+  const int grid = static_cast<int>(std::min<int64_t>((total + 255) / 256, 8192));
+  sf_tiles_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      sc.data_ptr<float>(), sc.stride(0), rows_per_group, tiles, KB, reinterpret_cast<uint32_t*>(out.data_ptr<uint8_t>()),
+      total);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
 // fp8 block-scaled grouped GEMM (forward shape): C[seg_g] = dequant(A)[seg_g] @ dequant(B[g])^T with
 // A [rows, K] e4m3 and B [G, N, K] e4m3, each with one power-of-two fp32 scale per (row,
 // 128-channel K block): sa [rows, K/128], sb [G, N, K/128]. Scales must be exact powers of two
@@ -845,15 +854,20 @@ void grouped_gemm_fp8_m(const at::Tensor& A, const at::Tensor& sa, const at::Ten
   a.M = static_cast<int>(A.size(0));
   TORCH_CHECK(A.size(1) == a.K && a.K % 128 == 0, "K mismatch, or K not a multiple of 128");
   const int64_t KB = a.K / 128;
-  TORCH_CHECK(sa.scalar_type() == at::kFloat && sa.dim() == 2 && sa.size(0) == A.size(0) && sa.size(1) == KB &&
-                  sa.stride(1) == 1,
-              "sa must be [rows, K/128] fp32");
-  TORCH_CHECK(sb.scalar_type() == at::kFloat && sb.is_contiguous() && sb.numel() == int64_t(a.G) * a.N * KB,
-              "sb must be [G, N, K/128] fp32");
-  a.sfa = sa.data_ptr<float>();
-  a.sfa_ld = sa.stride(0);
-  a.sfb = sb.data_ptr<float>();
-  a.sfb_ld = KB;
+  TORCH_CHECK(sa.scalar_type() == at::kByte ||
+                  (sa.scalar_type() == at::kFloat && sa.dim() == 2 && sa.size(0) == A.size(0) && sa.size(1) == KB &&
+                   sa.stride(1) == 1),
+              "sa must be [rows, K/128] fp32 (or its scale tiles)");
+  TORCH_CHECK(sb.scalar_type() == at::kByte ||
+                  (sb.scalar_type() == at::kFloat && sb.is_contiguous() && sb.numel() == int64_t(a.G) * a.N * KB),
+              "sb must be [G, N, K/128] fp32 (or its scale tiles)");
+  // scale tiles: given (uint8 [.., 512]) or built here from the fp32 scales
+  at::Tensor ta = sa.scalar_type() == at::kByte ? sa : sf_tiles(sa, 1, A.size(0));
+  at::Tensor tb = sb.scalar_type() == at::kByte ? sb : sf_tiles(sb.view({int64_t(a.G) * a.N, KB}), a.G, a.N);
+  TORCH_CHECK(ta.numel() == (A.size(0) + 127) / 128 * KB * 512 && tb.numel() == int64_t(a.G) * ((a.N + 127) / 128) * KB * 512,
+              "scale tiles have the wrong size");
+  a.sfa_tiles = ta.data_ptr<uint8_t>();
+  a.sfb_tiles = tb.data_ptr<uint8_t>();
   a.offsets = offsets.data_ptr<int64_t>();
   a.error = reinterpret_cast<uint32_t*>(error.data_ptr<int32_t>());
   a.timeout_ns = static_cast<uint64_t>(timeout_s * 1e9);

@@ -305,14 +305,19 @@ __global__ void __launch_bounds__(kPermCopyThreads) permute_copy_bulk_kernel(
 }
 
 // fp8 input (e4m3 rows with one fp32 scale per 128 channels, as an fp8 dispatch delivers
-// them): a warp per token reads the row once, dequantises 16 channels per lane-chunk to
-// bf16 and stores them to every destination slot of the token.
+// them): a warp per token reads the row once and stores it to every destination slot of the
+// token, either dequantised to bf16 (DEQUANT) or as e4m3 bytes plus the scales (for the fp8
+// GEMM; padding rows get zero bytes and scale 1).
+template <bool DEQUANT>
 __global__ void __launch_bounds__(256) permute_copy_fp8_kernel(const uint8_t* __restrict__ q, int64_t q_stride,
                                                                const float* __restrict__ sc, int64_t s_stride, int N,
                                                                int K, int H, const int32_t* __restrict__ pos,
-                                                               __nv_bfloat16* __restrict__ out,
+                                                               void* __restrict__ out_v, float* __restrict__ out_s,
                                                                const int64_t* __restrict__ offsets,
                                                                const int32_t* __restrict__ counts, int EL) {
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(out_v);
+  uint8_t* out_q = static_cast<uint8_t*>(out_v);
+  const int nsb = H / 128;
   const int lane = lane_id();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int GW = (gridDim.x * blockDim.x) >> 5;
@@ -327,6 +332,17 @@ __global__ void __launch_bounds__(256) permute_copy_fp8_kernel(const uint8_t* __
     if (np == 0) continue;
     const uint8_t* qr = q + static_cast<int64_t>(n) * q_stride;
     const float* sr = sc + static_cast<int64_t>(n) * s_stride;
+    if (!DEQUANT) {
+      for (int j = lane; j < nch; j += 32) {
+        const int4 v = reinterpret_cast<const int4*>(qr)[j];
+        for (int i = 0; i < np; ++i) reinterpret_cast<int4*>(out_q + static_cast<int64_t>(p[i]) * H)[j] = v;
+      }
+      for (int b = lane; b < nsb; b += 32) {
+        const float f = sr[b];
+        for (int i = 0; i < np; ++i) out_s[static_cast<int64_t>(p[i]) * nsb + b] = f;
+      }
+      continue;
+    }
     for (int j = lane; j < nch; j += 32) {
       const int4 v = reinterpret_cast<const int4*>(qr)[j];
       const float f = sr[j >> 3];  // 8 chunks of 16 per 128-channel block
@@ -345,19 +361,21 @@ __global__ void __launch_bounds__(256) permute_copy_fp8_kernel(const uint8_t* __
       }
     }
   }
-  const int64_t row_bytes = 2LL * H;
+  const int64_t row_bytes = DEQUANT ? 2LL * H : H;
   for (int e = 0; e < EL; ++e) {
     const int64_t s0 = offsets[e] + counts[e], t = offsets[e + 1];
     for (int64_t r = s0 + gw; r < t; r += GW) {
-      int4* d = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(out) + r * row_bytes);
+      int4* d = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(out_v) + r * row_bytes);
       for (int64_t i = lane; i < row_bytes / 16; i += 32) d[i] = make_int4(0, 0, 0, 0);
+      if (!DEQUANT)
+        for (int b = lane; b < nsb; b += 32) out_s[r * nsb + b] = 1.f;
     }
   }
 }
 
 void permute(const at::Tensor& x, const at::Tensor& ids, int64_t num_local_experts, at::Tensor out, at::Tensor pos,
              at::Tensor offsets, at::Tensor counts, at::Tensor scratch, const OptTensor& error,
-             const OptTensor& x_scales) {
+             const OptTensor& x_scales, const OptTensor& out_scales) {
   const c10::cuda::CUDAGuard guard(x.device());
   const int N = static_cast<int>(x.size(0)), K = static_cast<int>(ids.size(1)), EL = static_cast<int>(num_local_experts);
   TORCH_CHECK(EL <= kPermMaxExperts, "too many local experts");
@@ -384,15 +402,22 @@ void permute(const at::Tensor& x, const at::Tensor& ids, int64_t num_local_exper
   }
   const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
   if (x_scales.has_value()) {
-    TORCH_CHECK(x.element_size() == 1 && out.scalar_type() == at::kBFloat16 && out.size(1) == x.size(1) &&
-                    x.size(1) % 128 == 0 && x_scales->scalar_type() == at::kFloat && x_scales->stride(1) == 1 &&
+    const bool keep = out_scales.has_value();  // e4m3 rows + scales out, else bf16 rows
+    TORCH_CHECK(x.element_size() == 1 && out.size(1) == x.size(1) && x.size(1) % 128 == 0 &&
+                    x_scales->scalar_type() == at::kFloat && x_scales->stride(1) == 1 &&
                     x_scales->size(1) * 128 == x.size(1) && x.stride(0) % 16 == 0 &&
                     (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0,
-                "fp8 permute: x [N, H] e4m3 (H % 128 == 0, 16-byte aligned rows), scales [N, H/128] fp32, bf16 out");
-    permute_copy_fp8_kernel<<<sms * 4, 256, 0, s>>>(
-        static_cast<const uint8_t*>(x.data_ptr()), x.stride(0), x_scales->data_ptr<float>(), x_scales->stride(0), N, K,
-        static_cast<int>(x.size(1)), pos.data_ptr<int32_t>(), static_cast<__nv_bfloat16*>(out.data_ptr()),
-        offsets.data_ptr<int64_t>(), counts.data_ptr<int32_t>(), EL);
+                "fp8 permute: x [N, H] e4m3 (H % 128 == 0, 16-byte aligned rows), scales [N, H/128] fp32");
+    TORCH_CHECK(keep ? (out.element_size() == 1 && out_scales->scalar_type() == at::kFloat &&
+                        out_scales->is_contiguous() && out_scales->size(0) == out.size(0) &&
+                        out_scales->size(1) == x_scales->size(1))
+                     : out.scalar_type() == at::kBFloat16,
+                "fp8 permute: bf16 rows out, or e4m3 rows + [P, H/128] fp32 scales out");
+    auto kern = keep ? permute_copy_fp8_kernel<false> : permute_copy_fp8_kernel<true>;
+    kern<<<sms * 4, 256, 0, s>>>(static_cast<const uint8_t*>(x.data_ptr()), x.stride(0), x_scales->data_ptr<float>(),
+                                 x_scales->stride(0), N, K, static_cast<int>(x.size(1)), pos.data_ptr<int32_t>(),
+                                 out.data_ptr(), keep ? out_scales->data_ptr<float>() : nullptr,
+                                 offsets.data_ptr<int64_t>(), counts.data_ptr<int32_t>(), EL);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return;
   }

@@ -87,6 +87,7 @@ void fence_cost(SymmHeap& heap, int64_t peer, int64_t bytes, int64_t scope, at::
 void grouped_gemm_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, const OptTensor& C,
                     const OptTensor& Hout, int64_t epilogue, at::Tensor error, int64_t num_sms, double timeout_s,
                     bool b_kn, const OptTensor& residual);
+at::Tensor sf_tiles(const at::Tensor& sc, int64_t groups, int64_t rows_per_group);
 void grouped_gemm_fp8_m(const at::Tensor& A, const at::Tensor& sa, const at::Tensor& B, const at::Tensor& sb,
                         const at::Tensor& offsets, const OptTensor& C, const OptTensor& Hout, int64_t epilogue,
                         at::Tensor error, int64_t num_sms, double timeout_s);
@@ -98,7 +99,7 @@ void router_topk(const at::Tensor& logits, int64_t topk, at::Tensor idx, at::Ten
 void router_topk_bwd(const at::Tensor& idx, const at::Tensor& w, const at::Tensor& dw, at::Tensor dlogits);
 void permute(const at::Tensor& x, const at::Tensor& ids, int64_t num_local_experts, at::Tensor out, at::Tensor pos,
              at::Tensor offsets, at::Tensor counts, at::Tensor scratch, const OptTensor& error,
-             const OptTensor& x_scales);
+             const OptTensor& x_scales, const OptTensor& out_scales);
 void unpermute(const at::Tensor& rows, const at::Tensor& pos, const at::Tensor& w, at::Tensor y);
 void unpermute_bwd(const at::Tensor& dy, const at::Tensor& rows, const at::Tensor& pos, const at::Tensor& w,
                    at::Tensor drows, const OptTensor& dw, const at::Tensor& offsets, const at::Tensor& counts);

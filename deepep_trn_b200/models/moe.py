@@ -25,6 +25,7 @@ import torch.nn as nn
 
 from ..ops import gemm as G
 from ..ops import moe_ops as MO
+from ..ops.quant import quantize_fp8
 from ..utils.profiling import timer
 
 
@@ -119,7 +120,7 @@ class MoELayer(nn.Module):
 
     def __init__(self, buffer, hidden: int, intermediate: int, num_experts: int, topk: int,
                  dtype=torch.bfloat16, device=None, init_std: float = 0.02, seed: int = 0,
-                 fp8_dispatch: bool = False):
+                 fp8_dispatch: bool = False, fp8_experts: bool = False):
         super().__init__()
         R = buffer.group_size
         if num_experts % R:
@@ -128,6 +129,9 @@ class MoELayer(nn.Module):
             raise ValueError('hidden and intermediate must be multiples of 128')
         self.buffer = buffer
         self.fp8_dispatch = fp8_dispatch   # forward tokens cross NVLink as fp8 e4m3 + 1x128 scales
+        # inference (no autograd): fp8 dispatch and block-scaled fp8 expert GEMMs on e4m3 weights
+        self.fp8_experts = fp8_experts
+        self._fp8_cache = None
         self.hidden, self.intermediate = hidden, intermediate
         self.num_experts, self.topk = num_experts, topk
         EL = num_experts // R
@@ -149,7 +153,49 @@ class MoELayer(nn.Module):
         # e.g. a Zipf skew for benchmarks or a balancing bias)
         self.register_buffer('router_bias', torch.zeros(num_experts, dtype=torch.float32, device=device))
 
+    def _fp8_weights(self):
+        """e4m3 copies of the expert weights with power-of-two 1x128 scales (as scale tiles),
+        rebuilt when the weights change. W1 is re-interleaved in 64-row gate / up blocks, the
+        layout of the fp8 GEMM's 128-wide SwiGLU tiles."""
+        key = (self.w1._version, self.w2._version, self.w1.data_ptr(), self.w2.data_ptr())
+        if self._fp8_cache is None or self._fp8_cache[0] != key:
+            with torch.no_grad():
+                EL, I2, H = self.w1.shape
+                v = self.w1.reshape(EL, I2 // 256, 2, 128, H)
+                gate, up = v[:, :, 0].reshape(EL, I2 // 2, H), v[:, :, 1].reshape(EL, I2 // 2, H)
+                w1 = G.interleave_gate_up(gate, up, block=64)
+                q1, s1 = G.quantize_fp8_blocks(w1)
+                q2, s2 = G.quantize_fp8_blocks(self.w2)
+                self._fp8_cache = (key, q1, G.fp8_scale_tiles(s1, EL), q2, G.fp8_scale_tiles(s2, EL))
+        return self._fp8_cache[1:]
+
+    def _forward_fp8(self, x: torch.Tensor) -> torch.Tensor:
+        buf, E = self.buffer, self.num_experts
+        EL = E // buf.group_size
+        with timer.stage('moe.router'):
+            logits = router_logits(x, self.router) + self.router_bias
+            idx, w = MO.router_topk(logits, self.topk)
+        with timer.stage('moe.dispatch'):
+            ntr, _, nte, itr, _ = buf.get_dispatch_layout(idx, E)
+            recv_x, recv_idx, recv_w, per_expert, handle, _ = buf.dispatch(
+                x, topk_idx=idx, topk_weights=w, num_tokens_per_rank=ntr, is_token_in_rank=itr,
+                num_tokens_per_expert=nte, use_fp8=True, round_scale=True)
+        with timer.stage('moe.permute'):
+            (rq, rs), pos, offsets, _ = MO.permute(recv_x, recv_idx, EL, per_expert, keep_fp8=True)
+        q1, t1, q2, t2 = self._fp8_weights()
+        with timer.stage('moe.experts'):
+            h, _ = G.grouped_gemm_fp8(rq, rs, q1, t1, offsets, epilogue='swiglu', save_preact=False)
+            hq, hs = quantize_fp8(h, round_scale=True)
+            o = G.grouped_gemm_fp8(hq, hs, q2, t2, offsets)
+        with timer.stage('moe.unpermute'):
+            y_recv = MO.unpermute(o, pos, recv_w)
+        with timer.stage('moe.combine'):
+            y, _, _ = buf.combine(y_recv, handle)
+        return y
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.fp8_experts and not torch.is_grad_enabled():
+            return self._forward_fp8(x)
         return _MoEFunction.apply(x, self.router, self.w1, self.w2, self.buffer, self.num_experts, self.topk,
                                   self.router_bias, self.fp8_dispatch)
 

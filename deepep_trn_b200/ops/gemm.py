@@ -83,16 +83,28 @@ def quantize_fp8_blocks(w: torch.Tensor):
     return q.contiguous(), sc.contiguous()
 
 
+def fp8_scale_tiles(scales: torch.Tensor, groups: int = 1) -> torch.Tensor:
+    """Power-of-two fp32 scales [groups * rows, K/128] -> the 512-byte tiles ``grouped_gemm_fp8``
+    streams into tensor memory (one per 128 rows and 128-channel block). Build them once for
+    weights and pass the tiles instead of the fp32 scales to skip the per-call conversion."""
+    sc = scales.reshape(-1, scales.shape[-1]).float().contiguous()
+    return load().sf_tiles(sc, groups, sc.shape[0] // groups)
+
+
 def grouped_gemm_fp8(A, sa, B, sb, offsets, out=None, epilogue: str = 'bf16', h_out=None, save_preact: bool = True,
                      num_sms: int = 0, timeout_s: float = 10.0):
     """Block-scaled fp8 grouped GEMM on the tensor cores (``tcgen05.mma ... kind::mxf8f6f4.block_scale``):
     ``C[seg_e] = (A * sa)[seg_e] @ (B[e] * sb[e])^T`` with A [rows, K] and B [G, N, K] e4m3, and
-    power-of-two fp32 scales sa [rows, K/128], sb [G, N, K/128] (``quantize_fp8_blocks``).
+    power-of-two fp32 scales sa [rows, K/128], sb [G, N, K/128] (``quantize_fp8_blocks``), or
+    their ``fp8_scale_tiles``.
     fp32 accumulation; epilogues as ``grouped_gemm``. The SwiGLU epilogue reads each 128-wide
     output tile as [64 gate | 64 up] (``interleave_gate_up(..., block=64)``)."""
     rows, N = A.shape[0], B.shape[1]
     a8, b8 = A.view(torch.uint8), B.view(torch.uint8)
-    sa, sb = sa.float(), sb.float().contiguous()
+    if sa.dtype != torch.uint8:
+        sa = sa.float()
+    if sb.dtype != torch.uint8:
+        sb = sb.float().contiguous()
     if epilogue == 'swiglu':
         h = h_out if h_out is not None else torch.empty(rows, N // 2, dtype=torch.bfloat16, device=A.device)
         c = (out if out is not None else torch.empty(rows, N, dtype=torch.bfloat16, device=A.device)) \

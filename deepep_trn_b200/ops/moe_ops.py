@@ -41,11 +41,14 @@ def router_topk_bwd(idx: torch.Tensor, w: torch.Tensor, dw: torch.Tensor, num_ex
     return out
 
 
-def permute(x, local_ids: torch.Tensor, num_local_experts: int, counts: list[int] | None = None):
+def permute(x, local_ids: torch.Tensor, num_local_experts: int, counts: list[int] | None = None,
+            keep_fp8: bool = False):
     """Rows of ``x`` [N, H] grouped by local expert, each segment padded to a multiple of 128.
 
     ``x`` may also be an fp8 pair ``(x_e4m3 [N, H], scales [N, H/128] fp32)`` (what an fp8
-    dispatch delivers); the rows are then dequantised to bf16 on the way.
+    dispatch delivers); the rows are then dequantised to bf16 on the way, or, with
+    ``keep_fp8``, stay e4m3 and ``rows`` is the pair ``(rows_e4m3 [P, H], scales [P, H/128])``
+    (padding rows: zeros with scale 1), the operand of ``grouped_gemm_fp8``.
     Returns ``(rows [P, H], pos [N, K] int32, offsets [EL+1] int64, counts [EL] int32)``;
     ``pos[n, k]`` is the row of pair (n, k) or -1. ``counts`` (host list), when known,
     sizes ``rows`` exactly without a device synchronisation.
@@ -53,6 +56,8 @@ def permute(x, local_ids: torch.Tensor, num_local_experts: int, counts: list[int
     scales = None
     if isinstance(x, tuple):
         x, scales = x
+        if not x.is_cuda and keep_fp8:
+            raise NotImplementedError('keep_fp8 permute runs on CUDA tensors')
         if not x.is_cuda:
             from ..utils.codec import dequantize_fp8_1x128
             x, scales = dequantize_fp8_1x128(x, scales).to(torch.bfloat16), None
@@ -76,7 +81,10 @@ def permute(x, local_ids: torch.Tensor, num_local_experts: int, counts: list[int
                     fill[e] += 1
         return rows, pos, torch.tensor(offs, dtype=torch.int64), torch.tensor(counts, dtype=torch.int32)
     dev = x.device
-    rows = torch.empty(offs[-1], H, dtype=torch.bfloat16 if scales is not None else x.dtype, device=dev)
+    keep = keep_fp8 and scales is not None
+    rows = torch.empty(offs[-1], H, dtype=torch.uint8 if keep else (torch.bfloat16 if scales is not None else x.dtype),
+                       device=dev)
+    rows_s = torch.empty(offs[-1], H // 128, dtype=torch.float32, device=dev) if keep else None
     pos = torch.empty(N, K, dtype=torch.int32, device=dev)
     offsets = torch.empty(EL + 1, dtype=torch.int64, device=dev)
     cnt = torch.empty(EL, dtype=torch.int32, device=dev)
@@ -85,7 +93,9 @@ def permute(x, local_ids: torch.Tensor, num_local_experts: int, counts: list[int
     from .gemm import _err  # the kernels' shared device error word (timed-out copies)
     xq = x.view(torch.uint8) if scales is not None else x
     load().permute(xq, local_ids.contiguous(), EL, rows, pos, offsets, cnt, scratch, _err(dev),
-                   scales.float().contiguous() if scales is not None else None)
+                   scales.float().contiguous() if scales is not None else None, rows_s)
+    if keep:
+        return (rows.view(torch.float8_e4m3fn), rows_s), pos, offsets, cnt
     return rows, pos, offsets, cnt
 
 

@@ -158,7 +158,8 @@ def test_grouped_gemm_fp8_block_scaled(counts, N, K):
     qb, sb, B = _fp8_operand((G, N, K), g)
     o = torch.tensor(offs, dtype=torch.int64, device='cuda')
     C = grouped_gemm_fp8(qa, sa, qb, sb, o)
-    Cf = grouped_gemm_fp8(qa, sa, qb, sb, o, epilogue='f32')
+    from deepep_trn_b200.ops.gemm import fp8_scale_tiles
+    Cf = grouped_gemm_fp8(qa, sa, qb, fp8_scale_tiles(sb, G), o, epilogue='f32')   # prebuilt weight tiles
     torch.cuda.synchronize()
     check()
     for e in range(G):

@@ -134,3 +134,25 @@ def test_moe_layer_forward_backward_matches_fp32(fp8_dispatch):
     assert _rel(layer.router.grad, Wr.grad) < 8e-2 * tol, _rel(layer.router.grad, Wr.grad)
     buf.check()
     buf.destroy()
+
+
+@needs_cuda
+def test_moe_layer_fp8_experts_inference_matches_fp32():
+    # fp8 dispatch + block-scaled fp8 expert GEMMs (inference forward) against the fp32 layer
+    import torch.distributed as dist
+    from deepep_trn_b200 import Buffer
+    from deepep_trn_b200.models.moe import MoELayer, reference_moe
+    _init_single()
+    buf = Buffer(dist.group.WORLD, backend='nvlink', num_max_tokens_per_rank=512)
+    T, H, I, E, K = 384, 512, 256, 16, 4
+    layer = MoELayer(buf, H, I, E, K, device='cuda', init_std=0.05, fp8_experts=True)
+    x = (torch.randn(T, H, device='cuda') * 0.5).to(torch.bfloat16)
+    with torch.no_grad():
+        y = layer(x)
+        y2 = layer(x)   # weights cached in fp8 after the first call
+    torch.cuda.synchronize()
+    yr = reference_moe(x.float(), layer.router.float(), layer.w1.float(), layer.w2.float(), K)
+    assert _rel(y, yr) < 8e-2, _rel(y, yr)
+    assert torch.equal(y, y2)
+    buf.check()
+    buf.destroy()
