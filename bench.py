@@ -202,8 +202,8 @@ def main():
 
     # ---- low-latency: fp8 dispatch + bf16 combine of 128 tokens, CUDA-graph replay
     ll = None
-    if not args.no_ll and args.impl == 'ours':
-        ll = bench_ll(args, buf, rank, dev, control)
+    if not args.no_ll and args.impl in ('ours', 'nccl'):
+        ll = bench_ll(args, buf, rank, dev, control, graph=args.impl == 'ours')
 
     summaries = [None] * world
     dist.all_gather_object(summaries, clocks.summary(), group=control)
@@ -245,7 +245,9 @@ def profile_steps(fn, label, rank, n=3):
         log(prof.key_averages().table(sort_by='cuda_time_total', row_limit=15))
 
 
-def bench_ll(args, buf, rank, dev, control):
+def bench_ll(args, buf, rank, dev, control, graph: bool = True):
+    """fp8 low-latency dispatch + bf16 combine of ``--ll-tokens`` tokens. The NVLink kernels are
+    timed as CUDA-graph replays; the NCCL build (host-synchronised split sizes) as plain calls."""
     from deepep_trn_b200.utils.benchutil import max_over_ranks
     from deepep_trn_b200.utils.testing import randn_router
     T, E, H, K = args.ll_tokens, args.experts, args.hidden, args.topk
@@ -263,6 +265,17 @@ def bench_ll(args, buf, rank, dev, control):
     for _ in range(3):
         ll_step()
     torch.cuda.synchronize()
+    if not graph:
+        dist.barrier(group=control)
+        iters = 20
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        for _ in range(iters):
+            ll_step()
+        en.record()
+        torch.cuda.synchronize()
+        us = max_over_ranks(st.elapsed_time(en) * 1e3 / iters)
+        return {'tokens_per_rank': T, 'dispatch_fp8_plus_combine_us': round(us, 2), 'cuda_graph': False}
     if args.profile:
         profile_steps(ll_step, 'low-latency fp8 d + bf16 c', rank)
     graph = torch.cuda.CUDAGraph()

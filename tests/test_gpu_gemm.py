@@ -193,3 +193,26 @@ def test_grouped_gemm_fp8_swiglu():
         pg, pu = deinterleave(pre[s:t], block=64)
         _close(pg, gt)
         _close(pu, ut)
+
+
+@needs_cuda
+def test_custom_ops_on_cuda():
+    # the registered operators run the sm_100a kernels and trace into one graph
+    import torch._dynamo
+    import deepep_trn_b200.ops.library  # noqa: F401
+    ops = torch.ops.b200ep
+    torch.manual_seed(6)
+    A = (torch.randn(256, 512, device='cuda') * 0.5).to(torch.bfloat16)
+    B = (torch.randn(2, 256, 512, device='cuda') * 0.05).to(torch.bfloat16)
+    o = torch.tensor([0, 128, 256], dtype=torch.int64, device='cuda')
+    torch.library.opcheck(ops.grouped_gemm, (A, B, o, 'bf16', 'nk'))
+    torch.library.opcheck(ops.grouped_gemm_wgrad, (A, A, o, torch.bfloat16))
+
+    def f(A, B, o):
+        c = ops.grouped_gemm(A, B, o, 'f32', 'nk')
+        return ops.router_topk(c, 4)
+
+    torch._dynamo.reset()
+    got = torch.compile(f, fullgraph=True, backend='aot_eager')(A, B, o)
+    ref = f(A, B, o)
+    assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1])

@@ -120,3 +120,37 @@ def test_routers():
     logits = torch.tensor([[1.0, 3.0, 2.0, 3.0]])
     i, ww = router_topk_reference(logits, 2)
     assert sorted(i[0].tolist()) == [1, 3]
+
+
+def test_custom_ops_trace_without_graph_breaks():
+    """The kernels are registered as torch.ops.b200ep.* with fake implementations: they pass
+    torch.library.opcheck and compile with fullgraph=True (CPU definitions run here)."""
+    import torch._dynamo
+    import deepep_trn_b200.ops.library  # noqa: F401 - registers the operators
+    from deepep_trn_b200.ops import moe_ops as MO
+    ops = torch.ops.b200ep
+    g = torch.Generator().manual_seed(3)
+    logits = torch.randn(40, 16, generator=g)
+    torch.library.opcheck(ops.router_topk, (logits, 4))
+    idx, w = ops.router_topk(logits, 4)
+    torch.library.opcheck(ops.router_topk_bwd, (idx, w, torch.randn(40, 4, generator=g), 16))
+    x = torch.randn(40, 256, generator=g).to(torch.bfloat16)
+    torch.library.opcheck(ops.quantize_fp8, (x, True))
+    local = torch.where(idx < 8, idx, torch.full_like(idx, -1))   # experts 0..7 are local
+    rows, pos, offs, cnt = ops.permute(x, local, 8)
+    torch.library.opcheck(ops.unpermute, (rows, pos, w))
+    torch.library.opcheck(ops.permute_bwd, (rows, pos))
+
+    def layer(logits, x):
+        i, ww = ops.router_topk(logits, 4)
+        q, s = ops.quantize_fp8(x, True)
+        y = ops.unpermute(x.repeat_interleave(4, 0), torch.arange(160, dtype=torch.int32).reshape(40, 4), ww)
+        return i, y, s
+
+    torch._dynamo.reset()
+    compiled = torch.compile(layer, fullgraph=True, backend='aot_eager')
+    ref = layer(logits, x)
+    got = compiled(logits, x)
+    assert all(torch.equal(a, b) for a, b in zip(ref, got))
+    eg, _ = MO.router_topk(logits, 4)
+    assert torch.equal(eg, ref[0])
