@@ -125,8 +125,8 @@ def main():
             kw['use_fp8'] = True
         rx, ridx, rw, per_expert, handle, _ = buf.dispatch(x, **kw)
         if use_fp8:
-            from deepep_trn_b200.utils.codec import dequantize_fp8_1x128
-            rx = dequantize_fp8_1x128(*rx).to(torch.bfloat16)
+            from deepep_trn_b200.ops.quant import dequantize_fp8   # the identity expert reads fp8 in
+            rx = dequantize_fp8(*rx)
         out, ow, _ = buf.combine(rx, handle, topk_weights=None if args.no_combine_weights else rw)
         return out, ow, handle, itr
 

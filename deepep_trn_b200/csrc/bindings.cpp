@@ -44,6 +44,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ll_combine_send", &ll_combine_send);
   m.def("ll_combine_recv", &ll_combine_recv);
   m.def("quant_fp8", &quant_fp8);
+  m.def("dequant_fp8", &dequant_fp8);
   m.def("device_barrier", &device_barrier);
   m.def("grouped_gemm_m", &grouped_gemm_m);
   m.def("router_topk", &router_topk);

@@ -109,5 +109,6 @@ void transpose(const at::Tensor& in, at::Tensor out);
 
 // quant.cu
 void quant_fp8(const at::Tensor& x, at::Tensor q, at::Tensor scales, bool round_scale);
+void dequant_fp8(const at::Tensor& q, const at::Tensor& scales, at::Tensor out);
 
 }  // namespace b200ep

@@ -4,7 +4,7 @@ from __future__ import annotations
 
 import torch
 
-from ..utils.codec import quantize_fp8_1x128
+from ..utils.codec import dequantize_fp8_1x128, quantize_fp8_1x128
 from ._ext import load
 
 
@@ -17,3 +17,13 @@ def quantize_fp8(x: torch.Tensor, round_scale: bool = False):
     s = torch.empty(*x.shape[:-1], H // 128, dtype=torch.float32, device=x.device)
     load().quant_fp8(x, q.view(torch.uint8), s, round_scale)
     return q, s
+
+
+def dequantize_fp8(q: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """bf16 of e4m3 ``q`` [.., H] times its 1x128 fp32 ``scales`` [.., H/128] (one rounding)."""
+    if not q.is_cuda:
+        return dequantize_fp8_1x128(q, scales).to(torch.bfloat16)
+    q = q.contiguous()
+    out = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
+    load().dequant_fp8(q.view(torch.uint8), scales.float().contiguous(), out)
+    return out

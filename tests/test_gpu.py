@@ -59,6 +59,8 @@ def test_quant_kernel_bitwise(H, round_scale):
     rq, rs = quantize_fp8_1x128(x, round_scale)
     assert torch.equal(q.cpu().view(torch.uint8), rq.view(torch.uint8))
     assert torch.equal(s.cpu(), rs)
+    from deepep_trn_b200.ops.quant import dequantize_fp8
+    assert torch.equal(dequantize_fp8(q, s).cpu().view(torch.int16), dequantize_fp8(rq, rs).view(torch.int16))
 
 
 @needs_cuda
