@@ -166,6 +166,13 @@ class Buffer:
         """Per-phase device time (us) of the last normal-mode dispatch and combine (NVLink backend)."""
         return self._engine.device_trace() if hasattr(self._engine, 'device_trace') else {}
 
+    def check_canaries(self) -> None:
+        """Raise if any kernel wrote past the end of a region of this rank's symmetric heap
+        (guard zones filled with a known byte at construction; NVLink backend, a debugging aid
+        that synchronises the device)."""
+        if hasattr(self._engine, 'check_canaries'):
+            self._engine.check_canaries()
+
     def check(self) -> None:
         """Raise if a kernel of this buffer reported a device-side error (timeouts, capacity)."""
         if hasattr(self._engine, 'check'):

@@ -22,6 +22,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("status", &SymmHeap::status)
       .def("clear_status", &SymmHeap::clear_status)
       .def("trace", &SymmHeap::trace)
+      .def("check_canaries", &SymmHeap::check_canaries)
       .def("wait_notify", &SymmHeap::wait_notify, py::call_guard<py::gil_scoped_release>())
       .def_property_readonly("rank", &SymmHeap::rank)
       .def_property_readonly("world", &SymmHeap::world)

@@ -86,12 +86,22 @@ struct HeapLayout {
 
 __host__ __device__ inline int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
-inline HeapLayout make_layout(const HeapConfig& c) {
+// Every region is followed by a 256-byte guard zone that the host fills with kCanaryByte at
+// construction and checks on request (SymmHeap::check_canaries): a kernel that writes past
+// the end of a region, on any rank, changes it.
+constexpr int64_t kGuardBytes = 256;
+constexpr int kCanaryByte = 0xA5;
+
+inline HeapLayout make_layout(const HeapConfig& c, int64_t* guards = nullptr, int* nguards = nullptr) {
   HeapLayout L{};
   int64_t off = 0;
+  int ng = 0;
   auto take = [&](int64_t bytes) {
     int64_t o = off;
     off = align_up(off + bytes, 256);
+    if (guards != nullptr) guards[ng] = off;
+    ++ng;
+    off += kGuardBytes;
     return o;
   };
   L.sig = take(sizeof(Signals));
@@ -120,8 +130,10 @@ inline HeapLayout make_layout(const HeapConfig& c) {
   }
   for (int b = 0; b < 2; ++b) L.lc_rows[b] = take(int64_t(c.Mll) * c.K * 2LL * c.H);
   L.total = off;
+  if (nguards != nullptr) *nguards = ng;
   return L;
 }
+constexpr int kMaxGuards = 64;
 
 // What a kernel needs to reach every peer's heap. Passed by value.
 struct HeapView {

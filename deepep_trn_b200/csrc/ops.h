@@ -29,6 +29,8 @@ class SymmHeap {
   void clear_status();
   std::vector<int64_t> trace() const;
   std::vector<int64_t> wait_notify(uint64_t ticket, int num_local_experts, double timeout_s) const;
+  // Offsets (bytes into this rank's heap) of the guard zones whose canary bytes changed.
+  std::vector<int64_t> check_canaries() const;
 
   int rank() const { return rank_; }
   int world() const { return world_; }
@@ -42,6 +44,8 @@ class SymmHeap {
   int rank_, world_, device_, num_sms_ = 0;
   HeapConfig cfg_{};
   HeapLayout layout_{};
+  int64_t guards_[kMaxGuards] = {};
+  int nguards_ = 0;
   uint64_t timeout_ns_ = 0;
   void* local_ = nullptr;
   std::vector<void*> peers_;

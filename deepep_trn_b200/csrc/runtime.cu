@@ -27,11 +27,14 @@ SymmHeap::SymmHeap(int rank, int world, int M, int Mll, int H, int K, int E, int
   if (world < 1 || world > B200EP_MAX_RANKS) throw std::invalid_argument("EP group size must be in [1, 32]");
   if (rank < 0 || rank >= world) throw std::invalid_argument("rank out of range");
   cfg_ = HeapConfig{world, M, Mll, H, K, E};
-  layout_ = make_layout(cfg_);
+  layout_ = make_layout(cfg_, guards_, &nguards_);
+  if (nguards_ > kMaxGuards) throw std::logic_error("heap layout has more regions than guard slots");
   timeout_ns_ = static_cast<uint64_t>(timeout_s * 1e9);
   B200EP_CUDA_CHECK(cudaSetDevice(device));
   B200EP_CUDA_CHECK(cudaMalloc(&local_, static_cast<size_t>(layout_.total)));
   B200EP_CUDA_CHECK(cudaMemset(local_, 0, static_cast<size_t>(layout_.total)));
+  for (int i = 0; i < nguards_; ++i)
+    B200EP_CUDA_CHECK(cudaMemset(static_cast<uint8_t*>(local_) + guards_[i], kCanaryByte, kGuardBytes));
   B200EP_CUDA_CHECK(cudaHostAlloc(&host_, sizeof(HostPage), cudaHostAllocMapped));
   std::memset(host_, 0, sizeof(HostPage));
   B200EP_CUDA_CHECK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&host_dev_), host_, 0));
@@ -141,6 +144,23 @@ std::vector<int64_t> SymmHeap::wait_notify(uint64_t ticket, int num_local_expert
   for (int r = 0; r < world_; ++r) out.push_back(static_cast<int64_t>(n->recv_counts[r]));
   for (int e = 0; e < num_local_experts && e < 1024; ++e) out.push_back(static_cast<int64_t>(n->per_expert[e]));
   return out;
+}
+
+std::vector<int64_t> SymmHeap::check_canaries() const {
+  std::vector<int64_t> bad;
+  if (local_ == nullptr) return bad;
+  B200EP_CUDA_CHECK(cudaSetDevice(device_));
+  std::vector<uint8_t> zone(static_cast<size_t>(kGuardBytes));
+  for (int i = 0; i < nguards_; ++i) {
+    B200EP_CUDA_CHECK(cudaMemcpy(zone.data(), static_cast<const uint8_t*>(local_) + guards_[i],
+                                 static_cast<size_t>(kGuardBytes), cudaMemcpyDeviceToHost));
+    for (uint8_t b : zone)
+      if (b != static_cast<uint8_t>(kCanaryByte)) {
+        bad.push_back(guards_[i]);
+        break;
+      }
+  }
+  return bad;
 }
 
 }  // namespace b200ep

@@ -82,6 +82,15 @@ class NvlinkEngine:
             raise DeviceError(f'{ERRORS.get(code, "device error")} (code={code} op={op} rank={rank} '
                               f'peer={peer} expected={expected} seen={seen} aux={aux})')
 
+    def check_canaries(self) -> None:
+        """Raise if a guard zone between heap regions was overwritten (synchronises the device)."""
+        if self.heap is None:
+            return
+        torch.cuda.synchronize()
+        bad = self.heap.check_canaries()
+        if bad:
+            raise DeviceError(f'heap guard zones overwritten at byte offsets {bad} (rank {self.rank})')
+
     def device_trace(self) -> dict:
         """Phase durations (us) of the last normal-mode dispatch / combine on this rank, from
         %globaltimer stamps the kernels write into the heap (synchronises the device)."""

@@ -99,7 +99,21 @@ def main():
             (rq, rs), *_ = buf.dispatch((q.to(dev), s.to(dev)), handle=handle)
             eq, es = quantize_fp8_1x128(exp_x, round_scale=True)
             assert bitwise_equal(rq.cpu(), eq) and torch.equal(rs.cpu(), es), (kind, 'fp8 tuple dispatch')
+        if args.backend == 'nvlink' and kind == args.kinds.split(',')[0]:
+            # repeat-and-compare: the same dispatch / combine on 1..all SMs must give the same bits
+            # (an ordering race would show up as a difference between grid sizes)
+            from deepep_trn_b200 import Buffer
+            ident = (x.float() * ref_itr.sum(1, keepdim=True)).to(torch.bfloat16)
+            for n in (1, 3, 7, 16, 61, 0):
+                Buffer.set_num_sms(n)
+                rx2, _, _, _, h2, _ = buf.dispatch(d_x, topk_idx=d_idx, topk_weights=d_w, num_tokens_per_rank=ntr,
+                                                   is_token_in_rank=itr, num_tokens_per_expert=nte)
+                c2, _, _ = buf.combine(rx2, h2)
+                assert bitwise_equal(rx2.cpu(), recv_x), (kind, 'repeat dispatch', n)
+                assert torch.equal(c2.cpu(), ident), (kind, 'repeat combine', n)
+            Buffer.set_num_sms(0)
         buf.check()
+        buf.check_canaries()
         print(f'RANK={rank} intranode {kind}: T={T} sent={handle.send_counts.tolist()} '
               f'recv={handle.recv_counts.tolist()} expert_combine_rel={rel:.2e} PASS', flush=True)
     finish(control, buf)

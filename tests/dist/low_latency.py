@@ -91,6 +91,7 @@ def main():
                 assert torch.equal(out_g, eager), (kind, 'cuda graph replay')
             del g
         buf.check()
+        buf.check_canaries()
         print(f'RANK={rank} low_latency {kind}: T={T} recv_count_sum={int(rc.sum())} combine_rel={rel:.2e} PASS',
               flush=True)
     finish(control, buf)

@@ -96,7 +96,8 @@ def _ngpus():
 
 
 @needs_cuda
-@pytest.mark.parametrize('hidden,experts,topk,tokens,maxt', [(256, 32, 4, 24, 32), (7168, 256, 8, 96, 128)])
+@pytest.mark.parametrize('hidden,experts,topk,tokens,maxt', [(256, 32, 4, 24, 32), (7168, 256, 8, 96, 128),
+                                                           (128, 8, 1, 1, 4), (256, 16, 2, 3, 8)])
 def test_intranode_nvlink(run_dist, hidden, experts, topk, tokens, maxt):
     n = _ngpus()
     nproc = n if n in (1, 2, 4, 8) else 1
@@ -106,7 +107,8 @@ def test_intranode_nvlink(run_dist, hidden, experts, topk, tokens, maxt):
 
 
 @needs_cuda
-@pytest.mark.parametrize('hidden,experts,topk,tokens,maxt', [(256, 32, 4, 24, 32), (7168, 256, 8, 96, 128)])
+@pytest.mark.parametrize('hidden,experts,topk,tokens,maxt', [(256, 32, 4, 24, 32), (7168, 256, 8, 96, 128),
+                                                           (128, 8, 1, 1, 4), (256, 16, 2, 3, 8)])
 def test_low_latency_nvlink(run_dist, hidden, experts, topk, tokens, maxt):
     n = _ngpus()
     nproc = n if n in (1, 2, 4, 8) else 1
