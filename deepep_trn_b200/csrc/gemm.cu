@@ -817,7 +817,7 @@ __global__ void sf_tiles_kernel(const float* __restrict__ sc, int64_t ld, int64_
 
 at::Tensor sf_tiles(const at::Tensor& sc, int64_t groups, int64_t rows_per_group) {
   // sc: [groups * rows_per_group, KB] fp32 -> uint8 [groups, ceil(rows_per_group / 128), KB, 512]
-  TORCH_CHECK(sc.scalar_type() == at::kFloat && sc.dim() == 2 && sc.stride(1) == 1 &&
+  TORCH_CHECK(sc.scalar_type() == at::kFloat && sc.dim() == 2 && unit_inner(sc) &&
                   sc.size(0) == groups * rows_per_group,
               "scales must be [groups * rows, KB] fp32");
   const int KB = static_cast<int>(sc.size(1));
@@ -856,7 +856,7 @@ void grouped_gemm_fp8_m(const at::Tensor& A, const at::Tensor& sa, const at::Ten
   const int64_t KB = a.K / 128;
   TORCH_CHECK(sa.scalar_type() == at::kByte ||
                   (sa.scalar_type() == at::kFloat && sa.dim() == 2 && sa.size(0) == A.size(0) && sa.size(1) == KB &&
-                   sa.stride(1) == 1),
+                   unit_inner(sa)),
               "sa must be [rows, K/128] fp32 (or its scale tiles)");
   TORCH_CHECK(sb.scalar_type() == at::kByte ||
                   (sb.scalar_type() == at::kFloat && sb.is_contiguous() && sb.numel() == int64_t(a.G) * a.N * KB),

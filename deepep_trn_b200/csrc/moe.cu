@@ -404,7 +404,7 @@ void permute(const at::Tensor& x, const at::Tensor& ids, int64_t num_local_exper
   if (x_scales.has_value()) {
     const bool keep = out_scales.has_value();  // e4m3 rows + scales out, else bf16 rows
     TORCH_CHECK(x.element_size() == 1 && out.size(1) == x.size(1) && x.size(1) % 128 == 0 &&
-                    x_scales->scalar_type() == at::kFloat && x_scales->stride(1) == 1 &&
+                    x_scales->scalar_type() == at::kFloat && unit_inner(*x_scales) &&
                     x_scales->size(1) * 128 == x.size(1) && x.stride(0) % 16 == 0 &&
                     (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0,
                 "fp8 permute: x [N, H] e4m3 (H % 128 == 0, 16-byte aligned rows), scales [N, H/128] fp32");

@@ -302,7 +302,7 @@ void nd_prepare(SymmHeap& heap, const at::Tensor& x, const OptTensor& x_scales, 
   }
   if (mode == 1) {
     TORCH_CHECK(x.element_size() == 1 && x_scales.has_value(), "fp8 input needs (x_fp8, scales)");
-    TORCH_CHECK(x_scales->scalar_type() == at::kFloat && x_scales->stride(1) == 1, "scales must be fp32");
+    TORCH_CHECK(x_scales->scalar_type() == at::kFloat && unit_inner(*x_scales), "scales must be fp32");
     a.xs = x_scales->data_ptr<float>();
     a.xs_stride = x_scales->stride(0);
   }
@@ -1096,7 +1096,7 @@ void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const a
   TORCH_CHECK((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 || a.H % 8 != 0, "x must be 16-byte aligned");
   a.K = 0;
   if (w.has_value()) {
-    TORCH_CHECK(w->scalar_type() == at::kFloat && w->stride(1) == 1, "topk_weights must be fp32");
+    TORCH_CHECK(w->scalar_type() == at::kFloat && unit_inner(*w), "topk_weights must be fp32");
     a.w = w->data_ptr<float>();
     a.w_stride = w->stride(0);
     a.K = static_cast<int>(w->size(1));

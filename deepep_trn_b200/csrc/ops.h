@@ -56,6 +56,10 @@ class SymmHeap {
 
 using OptTensor = c10::optional<at::Tensor>;
 
+// Unit stride in the last dimension, or a last dimension of one element (whose stride torch
+// leaves arbitrary, e.g. the scales of a 128-wide fp8 row or top-1 routing weights).
+inline bool unit_inner(const at::Tensor& t) { return t.size(-1) <= 1 || t.stride(-1) == 1; }
+
 // layout.cu
 void layout(const at::Tensor& topk_idx, int64_t num_experts, int64_t num_ranks, at::Tensor ntr, at::Tensor nte,
             at::Tensor itr, at::Tensor scratch);
