@@ -68,6 +68,23 @@ def main():
                  r.get('error', '')] for r in bl]
         parts += ['## NCCL collective baselines', '',
                   table(['op', 'preset', 'EP', 'T/rank', 'pipelined us', 'latency us', 'error'], rows), '']
+    moe = load(run, 'moe')
+    if moe:
+        rows = []
+        for r in moe:
+            for impl in ('ours', 'nccl'):
+                if impl in r:
+                    rows.append([r.get('pass_', 'forward+backward'), r['ep'], r['experts'], r['tokens'],
+                                 r.get('dispatch_dtype', 'bf16'), r.get('expert_gemm_dtype', 'bf16'), impl,
+                                 r[impl]['ms_per_step'], r[impl]['tokens_per_s'], r[impl]['expert_tflops_per_rank']])
+        parts += ['## MoE layer (`bench/bench_moe.py`)', '',
+                  table(['pass', 'EP', 'experts', 'T/rank', 'dispatch', 'expert GEMMs', 'impl', 'ms/step', 'tokens/s',
+                         'expert TFLOP/s/rank'], rows), '']
+    gemm_file = run / 'gemm.jsonl'
+    if gemm_file.exists():
+        recs = [json.loads(line) for line in gemm_file.read_text().splitlines() if line.startswith('{')]
+        rows = [[k, v['ms'], v['tflops']] for r in recs for k, v in r.items() if isinstance(v, dict) and 'tflops' in v]
+        parts += ['## Grouped GEMM (`bench/bench_gemm.py`)', '', table(['GEMM', 'ms', 'TFLOP/s'], rows), '']
     (run / 'summary.md').write_text('\n'.join(parts))
     print(f'wrote {run / "summary.md"}')
 

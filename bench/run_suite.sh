@@ -20,5 +20,8 @@ else
   run bench/bench_ops.py --tokens 128,512,4096 --routings random,balanced,zipf,hot_rank0 --fp8 0,1
   run bench/bench_transport.py
   run bench/bench_baselines.py --tokens 128,512,4096
+  run bench/bench_moe.py --steps 5
+  run bench/bench_moe.py --steps 5 --forward-only --fp8 --impls ours
+  timeout -k 60 "$TIMEOUT" python bench/bench_gemm.py 2>&1 | tee -a "$OUT/gemm.jsonl"
 fi
 python bench/report.py "$OUT"

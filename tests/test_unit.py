@@ -154,3 +154,23 @@ def test_custom_ops_trace_without_graph_breaks():
     assert all(torch.equal(a, b) for a, b in zip(ref, got))
     eg, _ = MO.router_topk(logits, 4)
     assert torch.equal(eg, ref[0])
+
+
+def test_report_summarises_moe_and_gemm_records(tmp_path):
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    moe = dict(bench='moe', ep=8, tokens=4096, hidden=7168, inter=2048, experts=256, topk=8, routing='zipf',
+               ours=dict(ms_per_step=18.8, tokens_per_s=1.74e6, expert_tflops_per_rank=460.9),
+               nccl=dict(ms_per_step=33.1, tokens_per_s=0.99e6, expert_tflops_per_rank=261.8))
+    (tmp_path / 'moe_ep8.jsonl').write_text(json.dumps(moe) + '\n')
+    (tmp_path / 'gemm.jsonl').write_text('log line\n' + json.dumps(
+        dict(experts=32, gemm1_swiglu=dict(ms=1.5, tflops=1279.2), fp8_gemm2=dict(ms=0.63, tflops=1521.7))) + '\n')
+    p = subprocess.run([sys.executable, str(root / 'bench' / 'report.py'), str(tmp_path)], capture_output=True,
+                       text=True)
+    assert p.returncode == 0, p.stderr
+    text = (tmp_path / 'summary.md').read_text()
+    assert '## MoE layer' in text and '18.8' in text and '33.1' in text
+    assert 'fp8_gemm2' in text and '1521.7' in text
