@@ -208,7 +208,8 @@ def main():
     summaries = [None] * world
     dist.all_gather_object(summaries, clocks.summary(), group=control)
     clk = ClockSampler.merge(summaries)
-    launches = 4 * args.steps if args.impl == 'ours' else 0
+    # layout, prepare, pull, combine per step (+ the fp8 dequantisation of the identity expert)
+    launches = (5 if use_fp8 else 4) * args.steps if args.impl == 'ours' else 0
     if rank == 0:
         rec = {
             'metric': METRIC, 'value': round(value, 2), 'unit': 'GB/s (sum over GPUs)', 'n_gpus': world,
