@@ -166,6 +166,11 @@ def env_record() -> dict:
                                        capture_output=True, text=True, timeout=20).stdout.split('\n')[0].strip()
     except Exception:
         rec['driver'] = None
+    try:  # GPU interconnect matrix (NVLink / NVSwitch paths between the GPUs of the node)
+        topo = subprocess.run(['nvidia-smi', 'topo', '-m'], capture_output=True, text=True, timeout=20).stdout
+        rec['topo'] = topo.strip().splitlines()[:12] if topo else None
+    except Exception:
+        rec['topo'] = None
     try:
         rec['nccl'] = '.'.join(map(str, torch.cuda.nccl.version()))
     except Exception:
