@@ -90,3 +90,20 @@ def test_host_made_failures_raise(run_dist, case):
     else:
         assert rc == 0 and len(status) == 3, out[-3000:]
         assert any(s == 'DETECTED=RuntimeError' for s in status.values()), out[-3000:]
+
+
+def test_transport_probe_gloo(tmp_path):
+    """bench/probe_transport.py: an empty peer and a full-capacity peer, reported as PROBE json."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+    from conftest import free_port
+    root = Path(__file__).resolve().parents[1]
+    cmd = [sys.executable, '-m', 'torch.distributed.run', '--nnodes', '1', '--nproc-per-node', '2',
+           '--master-addr', '127.0.0.1', '--master-port', str(free_port()), str(root / 'bench' / 'probe_transport.py'),
+           '--backend', 'gloo']
+    p = subprocess.run(['timeout', '-k', '30', '300', *cmd], capture_output=True, text=True, cwd=str(root))
+    recs = [json.loads(line[len('PROBE '):]) for line in p.stdout.splitlines() if line.startswith('PROBE ')]
+    assert p.returncode == 0 and len(recs) == 2, p.stdout[-2000:] + p.stderr[-2000:]
+    assert all(r['status'] == 'pass' for r in recs) and sorted(r['tokens'] for r in recs) == [0, 64]

@@ -139,3 +139,17 @@ def test_absent_peer_times_out_cleanly(run_dist, case):
     # rank 1 skips the op; rank 0's bounded waits must turn into a DeviceError within seconds
     rc, out = run_dist('peer_absent.py', 2, '--case', case, timeout=300, env={'NCCL_NVLS_ENABLE': '0'})
     assert rc == 0 and 'PEER_ABSENT_PASS' in out, out[-6000:]
+
+
+@needs_cuda
+def test_transport_probe_nvlink():
+    # an empty peer and a full-capacity peer through the NVLink kernels (one rank per GPU, up to 2)
+    import json
+    n = min(2, _ngpus())
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cmd = [sys.executable, '-m', 'torch.distributed.run', '--nnodes', '1', '--nproc-per-node', str(n),
+           '--master-addr', '127.0.0.1', '--master-port', str(__import__('conftest').free_port()),
+           os.path.join(root, 'bench', 'probe_transport.py'), '--backend', 'nvlink']
+    p = subprocess.run(['timeout', '-k', '30', '300', *cmd], capture_output=True, text=True, cwd=root)
+    recs = [json.loads(line[len('PROBE '):]) for line in p.stdout.splitlines() if line.startswith('PROBE ')]
+    assert p.returncode == 0 and len(recs) == n and all(r['status'] == 'pass' for r in recs), p.stdout[-3000:]
