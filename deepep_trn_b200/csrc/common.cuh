@@ -14,6 +14,23 @@
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 
+#include <atomic>
+
+// Sets a kernel's dynamic shared-memory limit once per device. The attribute belongs to the
+// device's context, so a process that drives several GPUs must set it on each of them;
+// `seen` keeps one bit per device (setting it twice, from two threads, is harmless).
+template <typename Fn>
+inline cudaError_t set_smem_limit_once(std::atomic<uint64_t>& seen, Fn fn, int bytes) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+  if (bit != 0 && (seen.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err == cudaSuccess) seen.fetch_or(bit, std::memory_order_release);
+  return err;
+}
+
 #ifndef B200EP_MAX_RANKS
 #define B200EP_MAX_RANKS 32
 #endif

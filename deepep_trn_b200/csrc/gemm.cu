@@ -677,11 +677,8 @@ void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
   constexpr size_t smem = 1024 + STAGES * Smem<BN>::kStageBytes + kEpiBytes +
                           (FP8 ? STAGES * sf_stage_bytes<BN>() : 0) + (2 * STAGES + 5) * 8 + 16;
   auto kfn = grouped_gemm_kernel<GROUP_K, BN, STAGES, EPI, LAYOUT, FP8>;
-  static bool set = false;
-  if (!set) {
-    AT_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    set = true;
-  }
+  static std::atomic<uint64_t> seen{0};
+  AT_CUDA_CHECK(set_smem_limit_once(seen, kfn, static_cast<int>(smem)));
   kfn<<<grid, kThreads, smem, stream>>>(ma, mb, mc, mh, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -429,12 +429,8 @@ void permute(const at::Tensor& x, const at::Tensor& ids, int64_t num_local_exper
     const int stage_bytes = static_cast<int>((row_bytes + 127) / 128 * 128);
     const int nstages = static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(8, (96 * 1024) / stage_bytes)));
     const size_t smem = static_cast<size_t>(nstages) * stage_bytes + nstages * 8;
-    static bool attr = false;
-    if (!attr) {
-      AT_CUDA_CHECK(cudaFuncSetAttribute(permute_copy_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         200 * 1024));
-      attr = true;
-    }
+    static std::atomic<uint64_t> seen{0};
+    AT_CUDA_CHECK(set_smem_limit_once(seen, permute_copy_bulk_kernel, 200 * 1024));
     const int grid = std::max(1, std::min(N, sms * 2));
     permute_copy_bulk_kernel<<<grid, kPermCopyThreads, smem, s>>>(
         static_cast<const uint8_t*>(x.data_ptr()), xs, N, K, row_bytes, pos.data_ptr<int32_t>(),

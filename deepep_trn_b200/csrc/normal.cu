@@ -550,11 +550,8 @@ void nd_pull(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_scales, co
     a.nstages = static_cast<int>(std::max<int64_t>(2, std::min<int64_t>(16, budget / a.stage_bytes)));
     smem = static_cast<size_t>(a.nstages) * a.stage_bytes + a.nstages * sizeof(uint64_t);
     TORCH_CHECK(smem <= 200 * 1024, "row too large for the TMA pipeline");
-    static bool attr_set = false;
-    if (!attr_set) {
-      cudaFuncSetAttribute(nd_pull_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
-      attr_set = true;
-    }
+    static std::atomic<uint64_t> seen{0};
+    AT_CUDA_CHECK(set_smem_limit_once(seen, nd_pull_kernel, 220 * 1024));
   }
   const int grid = num_sms > 0 ? static_cast<int>(num_sms) : heap.num_sms();
   nd_pull_kernel<<<grid, kPullThreads, smem, at::cuda::getCurrentCUDAStream()>>>(a);
@@ -1141,12 +1138,8 @@ void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const a
     const size_t psmem = static_cast<size_t>(p.nstages) * p.stage_bytes + p.nstages * 16;
     void* pfn = x.scalar_type() == at::kHalf ? reinterpret_cast<void*>(nc_pull_kernel<__half>)
                                              : reinterpret_cast<void*>(nc_pull_kernel<__nv_bfloat16>);
-    static bool pattr[2] = {false, false};
-    const int pw = x.scalar_type() == at::kHalf ? 1 : 0;
-    if (!pattr[pw]) {
-      AT_CUDA_CHECK(cudaFuncSetAttribute(pfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-      pattr[pw] = true;
-    }
+    static std::atomic<uint64_t> pseen[2];
+    AT_CUDA_CHECK(set_smem_limit_once(pseen[x.scalar_type() == at::kHalf ? 1 : 0], pfn, 200 * 1024));
     int per_sm = 0;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pfn, kCombThreads, psmem);
     const int g = std::max(1, std::min(grid, per_sm * heap.num_sms()));
@@ -1163,12 +1156,8 @@ void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const a
   if (const char* v = getenv("B200EP_PUSH_STAGES")) a.nstages = std::max(2, std::min(16, atoi(v)));
   while (static_cast<int64_t>(a.nstages) * a.chunk_bytes > 150 * 1024 && a.nstages > 2) --a.nstages;
   const size_t smem = a.use_tma ? static_cast<size_t>(a.nstages) * a.chunk_bytes + a.nstages * 8 : 0;
-  static bool attr_set[2] = {false, false};
-  const int which = x.scalar_type() == at::kHalf ? 1 : 0;
-  if (!attr_set[which]) {
-    AT_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024));
-    attr_set[which] = true;
-  }
+  static std::atomic<uint64_t> seen[2];
+  AT_CUDA_CHECK(set_smem_limit_once(seen[x.scalar_type() == at::kHalf ? 1 : 0], kfn, 160 * 1024));
   int per_sm = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kCombThreads, smem);
   grid = std::max(1, std::min(grid, per_sm * heap.num_sms()));
