@@ -62,7 +62,6 @@ class BaselineMoELayer(nn.Module):
 
     def forward(self, x):
         EL = self.w1.shape[0]
-        lo = self.buffer.rank * EL
         logits = (x.float() @ self.router.float().t()) + self.router_bias
         vals, idx = torch.topk(logits, self.topk, dim=-1)
         w = torch.softmax(vals, -1)

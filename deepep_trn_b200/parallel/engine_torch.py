@@ -145,7 +145,6 @@ class TorchEngine:
         EL = experts_per_rank(num_experts, R)
         lo, K = self.rank * EL, idx.shape[1]
         with timer.stage('plan'):
-            owner = rank_of_expert(idx, num_experts, R)
             in_rank = token_rank_mask(idx, num_experts, R)
             token, counts = send_plan(in_rank)
         with timer.stage('pack'):

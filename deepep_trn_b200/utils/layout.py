@@ -86,7 +86,7 @@ def pair_plan(owner: torch.Tensor, num_ranks: int):
     (reference deep_ep_trn/layout.py:39-51). Vectorised with a stable sort instead
     of a loop over ranks.
     """
-    T, K = owner.shape
+    K = owner.shape[1]
     dst = owner.reshape(-1)
     keep = (dst >= 0).nonzero().flatten()
     # flat index t*K+k is already (token, k) ordered, so a stable sort on dst suffices

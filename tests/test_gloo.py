@@ -107,3 +107,24 @@ def test_transport_probe_gloo(tmp_path):
     recs = [json.loads(line[len('PROBE '):]) for line in p.stdout.splitlines() if line.startswith('PROBE ')]
     assert p.returncode == 0 and len(recs) == 2, p.stdout[-2000:] + p.stderr[-2000:]
     assert all(r['status'] == 'pass' for r in recs) and sorted(r['tokens'] for r in recs) == [0, 64]
+
+
+def test_baseline_moe_layer_cpu(single_rank_group):
+    """The NCCL + grouped-matmul baseline layer (here over gloo on CPU) against the fp32 definition."""
+    from deepep_trn_b200 import Buffer
+    from deepep_trn_b200.models.moe import reference_moe
+    from deepep_trn_b200.models.moe_baseline import BaselineMoELayer
+    buf = Buffer(single_rank_group, backend='gloo', num_max_tokens_per_rank=64)
+    T, H, I, E, K = 48, 256, 128, 8, 2
+    layer = BaselineMoELayer(buf, H, I, E, K)
+    torch.manual_seed(0)
+    with torch.no_grad():
+        for p in layer.parameters():
+            p.normal_(0, 0.05)
+    x = (torch.randn(T, H) * 0.5).to(torch.bfloat16).requires_grad_()
+    y = layer(x)
+    yr = reference_moe(x.detach().float(), layer.router.detach().float(), layer.w1.detach().float(),
+                       layer.w2.detach().float(), K)
+    assert ((y.float() - yr).norm() / yr.norm()).item() < 2e-2
+    y.float().square().sum().backward()
+    assert x.grad is not None and torch.isfinite(x.grad.float()).all() and layer.w1.grad.abs().sum() > 0
