@@ -36,6 +36,37 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("heap_bytes", [](int R, int M, int Mll, int H, int K, int E) {
     return make_layout(HeapConfig{R, M, Mll, H, K, E}).total;
   });
+  // The symmetric-heap layout for a configuration: region offsets, guard-zone offsets, total.
+  m.def("heap_layout", [](int R, int M, int Mll, int H, int K, int E) {
+    int64_t guards[kMaxGuards] = {};
+    int ng = 0;
+    const HeapLayout L = make_layout(HeapConfig{R, M, Mll, H, K, E}, guards, &ng);
+    py::dict d;
+    d["sig"] = L.sig;
+    d["local"] = L.local;
+    d["row_stride"] = L.row_stride;
+    auto pair = [](const int64_t (&v)[2]) { return py::make_tuple(v[0], v[1]); };
+    d["nd_x"] = pair(L.nd_x);
+    d["nd_topk"] = pair(L.nd_topk);
+    d["nd_w"] = pair(L.nd_w);
+    d["nd_lists"] = pair(L.nd_lists);
+    d["nd_counts"] = pair(L.nd_counts);
+    d["nd_nte"] = pair(L.nd_nte);
+    d["nc_rows"] = pair(L.nc_rows);
+    d["nc_w"] = pair(L.nc_w);
+    d["nc_send"] = pair(L.nc_send);
+    d["nc_send_w"] = pair(L.nc_send_w);
+    d["nc_send_off"] = pair(L.nc_send_off);
+    d["ll_rows"] = pair(L.ll_rows);
+    d["ll_ids"] = pair(L.ll_ids);
+    d["lc_rows"] = pair(L.lc_rows);
+    d["guards"] = std::vector<int64_t>(guards, guards + ng);
+    d["guard_bytes"] = kGuardBytes;
+    d["signals_bytes"] = static_cast<int64_t>(sizeof(Signals));
+    d["local_state_bytes"] = static_cast<int64_t>(sizeof(LocalState));
+    d["total"] = L.total;
+    return d;
+  });
   m.def("layout", &layout);
   m.def("nd_prepare", &nd_prepare);
   m.def("nd_pull", &nd_pull);

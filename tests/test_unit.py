@@ -174,3 +174,31 @@ def test_report_summarises_moe_and_gemm_records(tmp_path):
     text = (tmp_path / 'summary.md').read_text()
     assert '## MoE layer' in text and '18.8' in text and '33.1' in text
     assert 'fp8_gemm2' in text and '1521.7' in text
+
+
+@pytest.mark.parametrize('R,M,Mll,H,K,E', [(1, 4, 1, 128, 1, 8), (8, 4096, 128, 7168, 8, 256), (3, 100, 7, 384, 6, 30)])
+def test_heap_layout_regions_fit_and_guards_separate_them(R, M, Mll, H, K, E):
+    """The symmetric heap's layout (computed by the C++ runtime, no GPU needed): every region has
+    room for what the kernels put there, starts 256-byte aligned, and is followed by its own
+    guard zone before the next region begins."""
+    from deepep_trn_b200.ops._ext import available, load
+    if not available():
+        pytest.skip('extension not built')
+    L = load().heap_layout(R, M, Mll, H, K, E)
+    rs = L['row_stride']
+    assert rs >= 2 * H and rs % 16 == 0
+    need = {'nd_x': M * rs, 'nd_topk': M * K * 4, 'nd_w': M * K * 4, 'nd_lists': R * M * 4, 'nd_counts': R * 4,
+            'nd_nte': E * 4, 'nc_rows': R * M * 2 * H, 'nc_w': R * M * K * 4, 'nc_send': R * M * 2 * H,
+            'nc_send_w': R * M * K * 4, 'nc_send_off': (R + 1) * 8, 'll_rows': R * Mll * rs, 'll_ids': R * Mll * K * 4,
+            'lc_rows': Mll * K * 2 * H}
+    regions = [(L['sig'], L['signals_bytes']), (L['local'], L['local_state_bytes'])]
+    regions += [(off, need[name]) for name in need for off in L[name]]
+    regions.sort()
+    guards = sorted(L['guards'])
+    gb = L['guard_bytes']
+    assert len(guards) == len(regions)
+    for (off, size), g in zip(regions, guards):
+        assert off % 256 == 0 and off + size <= g, (off, size, g)     # the region fits before its guard
+    for (g, (nxt, _)) in zip(guards, regions[1:]):
+        assert g + gb <= nxt                                          # the guard ends before the next region
+    assert guards[-1] + gb <= L['total']
