@@ -69,6 +69,13 @@ def main():
             got = combined.cpu().float()
             rel = float((got - ref).abs().mean() / ref.abs().mean().clamp_min(1e-9)) if T else 0.0
             assert torch.allclose(got, ref, rtol=1e-2, atol=1e-3) and rel < 5e-3, (kind, fp8, rel)
+            if not fp8 and K <= 2 and args.backend == 'gloo':
+                # identity experts on the CPU path: out == sum_k w_k * x exactly (two fp32 products, one
+                # sum, one cast; the GPU kernels may fuse the multiply-add, so they keep the tolerance above)
+                ident, _, _ = buf.low_latency_combine(recv_x, idx.to(dev), w.to(dev), handle)
+                wk = w * (idx >= 0)
+                exact = sum(x.float() * wk[:, k:k + 1] for k in range(K)).to(torch.bfloat16)
+                assert torch.equal(ident.cpu(), exact), (kind, 'identity combine exact')
         if args.graph and args.backend == 'nvlink':
             # capture dispatch -> expert -> combine once, replay, and compare to the eager result
             d_x, d_idx, d_w = x.to(dev), idx.to(dev), w.to(dev)

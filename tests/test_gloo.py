@@ -65,6 +65,13 @@ def test_low_latency_gloo(run_dist, ep):
     assert rc == 0 and 'LOW_LATENCY_PASS' in out, out[-4000:]
 
 
+def test_low_latency_roundtrip_exact_gloo(run_dist):
+    # world 2, T=64, H=256, E=8, K=2: identity experts give out == sum_k w_k * x exactly
+    rc, out = run_dist('low_latency.py', 2, '--backend', 'gloo', '--hidden', 256, '--experts', 8, '--topk', 2,
+                       '--tokens', 64, '--max-tokens', 64, timeout=600)
+    assert rc == 0 and 'LOW_LATENCY_PASS' in out, out[-4000:]
+
+
 REF = __import__('pathlib').Path(__file__).resolve().parents[1] / 'baseline' / '_ref' / 'deep_ep_trn'
 
 
