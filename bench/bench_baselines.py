@@ -11,18 +11,18 @@ EP group, timed with CUDA events (max over ranks):
 
 torchrun --nnodes 1 --nproc-per-node 8 --master-addr 127.0.0.1 bench/bench_baselines.py
 """
-from common import PRESETS, Ctx, append_jsonl, base_parser
+from harness import PRESETS, BenchGroup, cli, device_stats, write_jsonl
 
 import torch
 import torch.distributed as dist
 
 
 def main():
-    args = base_parser(__doc__).parse_args()
+    args = cli(__doc__).parse_args()
     if args.backend == 'gloo':
         raise SystemExit('baselines run over NCCL on the GPUs')
-    ctx = Ctx('nccl', args.ep)
-    g, R = ctx.ep_group, ctx.ep
+    ctx = BenchGroup('nccl', args.ep)
+    g, R = ctx.group, ctx.ep
 
     def ops(T, H):
         dev = ctx.device
@@ -44,16 +44,16 @@ def main():
             for name, fn in ops(T, H).items():
                 rec = dict(bench='baseline', op=name, preset=preset, hidden=H, ep=R, tokens=T)
                 try:
-                    rec['device_us'] = ctx.measure(fn, args.rounds, args.iters)
-                    rec['latency_us'] = ctx.measure(fn, args.rounds, args.iters, sync_each=True)
+                    rec['device_us'] = device_stats(ctx, fn, args.rounds, args.iters)
+                    rec['latency_us'] = device_stats(ctx, fn, args.rounds, args.iters, each=True)
                 except Exception as exc:  # an unsupported collective is a result, not a crash
                     rec['error'] = f'{type(exc).__name__}: {str(exc).splitlines()[0][:300]}'
                 if ctx.rank == 0:
-                    append_jsonl(args.out_dir / f'baselines_ep{R}.jsonl', rec)
+                    write_jsonl(args.out_dir / f'baselines_ep{R}.jsonl', rec)
                     val = (f"{rec['device_us']['median_us']}us latency={rec['latency_us']['median_us']}us"
                            if 'device_us' in rec else rec['error'])
                     print(f'[baseline] {name} {preset} ep={R} T={T}: {val}', flush=True)
-    ctx.finish()
+    ctx.close()
 
 
 if __name__ == '__main__':

@@ -8,7 +8,7 @@ ranks, L2 flushed between steps.
 
 torchrun --nnodes 1 --nproc-per-node 8 --master-addr 127.0.0.1 bench/bench_moe.py
 """
-from common import Ctx, append_jsonl, base_parser
+from harness import BenchGroup, cli, write_jsonl
 
 import json
 
@@ -26,7 +26,7 @@ def zipf_bias(E: int, seed: int = 12345) -> torch.Tensor:
 
 
 def main():
-    p = base_parser(__doc__)
+    p = cli(__doc__)
     p.add_argument('--hidden', type=int, default=7168)
     p.add_argument('--inter', type=int, default=2048)
     p.add_argument('--experts', type=int, default=256)
@@ -41,7 +41,7 @@ def main():
     p.set_defaults(tokens=[4096])
     args = p.parse_args()
     T = args.tokens[0]
-    ctx = Ctx('nccl', args.ep)
+    ctx = BenchGroup('nccl', args.ep)
     from deepep_trn_b200 import Buffer
     from deepep_trn_b200.models.moe import MoELayer
     from deepep_trn_b200.models.moe_baseline import BaselineMoELayer
@@ -50,7 +50,7 @@ def main():
     results = {}
     params = None   # the first layer's parameters, copied into the others
     for impl in args.impls.split(','):
-        buf = Buffer(ctx.ep_group, backend='nvlink' if impl == 'ours' else 'nccl', num_max_tokens_per_rank=T,
+        buf = Buffer(ctx.group, backend='nvlink' if impl == 'ours' else 'nccl', num_max_tokens_per_rank=T,
                      hidden=H, num_experts=E, topk=K)
         layer = (MoELayer(buf, H, I, E, K, device=dev, init_std=0.02, seed=7, fp8_dispatch=args.fp8,
                           fp8_experts=args.fp8 and args.forward_only) if impl == 'ours'
@@ -87,7 +87,7 @@ def main():
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize()
-        dist.barrier(group=ctx.control)
+        dist.barrier(group=ctx.meta)
         timer = DeviceTimer()
         for _ in range(args.steps):
             timer.run(step)
@@ -118,9 +118,9 @@ def main():
     if 'ours' in results and 'nccl' in results:
         rec['speedup_vs_nccl_cublas'] = round(results['nccl']['ms_per_step'] / results['ours']['ms_per_step'], 3)
     if ctx.rank == 0:
-        append_jsonl(args.out_dir / f'moe_ep{ctx.ep}.jsonl', rec)
+        write_jsonl(args.out_dir / f'moe_ep{ctx.ep}.jsonl', rec)
         print(json.dumps(rec), flush=True)
-    ctx.finish()
+    ctx.close()
 
 
 if __name__ == '__main__':

@@ -41,11 +41,9 @@ def main():
              'Device time (CUDA events), max over ranks, median of rounds. Logical bytes follow deep_ep '
              '(normal: received rows x H x 2; LL: selected experts x H x 2).', '']
     if ops:
-        rows = [[r['mode'], r['preset'], r['ep'], r['tokens'], r['routing'], r.get('fp8'),
-                 'PASS' if r['check']['passed'] else 'FAIL', med(r['device_us']['dispatch']),
-                 med(r['device_us']['combine']), med(r['device_us']['dispatch_combine']),
-                 med(r['latency_us']['dispatch']), med(r['latency_us']['combine']),
-                 r['gbps_per_rank']['dispatch_combine'], r['recv_load']['imbalance']]
+        rows = [[r['mode'], r['preset'], r['ep'], r['tokens'], r['routing'], r.get('fp8'), r['check'],
+                 med(r['send_us']), med(r['back_us']), med(r['both_us']), med(r['send_latency_us']),
+                 med(r['back_latency_us']), r['gbps_per_rank']['both'], r['rows']['imbalance']]
                 for r in sorted(ops, key=lambda r: (r['mode'], r['preset'], r['ep'], r['tokens'], r['routing']))]
         parts += ['## Ops', '', table(['mode', 'preset', 'EP', 'T/rank', 'routing', 'fp8', 'check', 'dispatch us',
                                        'combine us', 'd+c us', 'latency d us', 'latency c us', 'GB/s/rank d+c',
@@ -55,14 +53,13 @@ def main():
             w.writerow(['mode', 'preset', 'ep', 'tokens', 'routing', 'fp8', 'check', 'dispatch_us', 'combine_us',
                         'dc_us', 'gbps_rank_dc'])
             for r in ops:
-                w.writerow([r['mode'], r['preset'], r['ep'], r['tokens'], r['routing'], r.get('fp8'),
-                            r['check']['passed'], med(r['device_us']['dispatch']), med(r['device_us']['combine']),
-                            med(r['device_us']['dispatch_combine']), r['gbps_per_rank']['dispatch_combine']])
+                w.writerow([r['mode'], r['preset'], r['ep'], r['tokens'], r['routing'], r.get('fp8'), r['check'],
+                            med(r['send_us']), med(r['back_us']), med(r['both_us']), r['gbps_per_rank']['both']])
     if tr:
-        rows = [[r['ep'], r['hidden'], r['rows_per_peer'], r['fill'], r['tma'], med(r['device_us']),
-                 r['payload_gbps'], r['off_rank_gbps']] for r in tr]
-        parts += ['## Transport (dispatch pull) curve', '',
-                  table(['EP', 'H', 'rows/peer', 'fill', 'tma', 'us', 'payload GB/s', 'off-rank GB/s'], rows), '']
+        rows = [[r['ep'], r['engine'], r['chunk'], r['mib_per_peer'], med(r['device_us']), r['gbps_per_gpu']]
+                for r in tr]
+        parts += ['## NVLink engines (all-to-all, every rank to every peer at once)', '',
+                  table(['EP', 'engine', 'bytes/transfer', 'MiB/peer', 'us', 'off-rank GB/s per GPU'], rows), '']
     if bl:
         rows = [[r['op'], r['preset'], r['ep'], r['tokens'], med(r.get('device_us')), med(r.get('latency_us')),
                  r.get('error', '')] for r in bl]

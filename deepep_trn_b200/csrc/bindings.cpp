@@ -23,6 +23,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("clear_status", &SymmHeap::clear_status)
       .def("trace", &SymmHeap::trace)
       .def("check_canaries", &SymmHeap::check_canaries)
+      .def("reset_counters", &SymmHeap::reset_counters)
       .def("wait_notify", &SymmHeap::wait_notify, py::call_guard<py::gil_scoped_release>())
       .def_property_readonly("rank", &SymmHeap::rank)
       .def_property_readonly("world", &SymmHeap::world)
@@ -46,17 +47,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     d["local"] = L.local;
     d["row_stride"] = L.row_stride;
     auto pair = [](const int64_t (&v)[2]) { return py::make_tuple(v[0], v[1]); };
-    d["nd_x"] = pair(L.nd_x);
-    d["nd_topk"] = pair(L.nd_topk);
-    d["nd_w"] = pair(L.nd_w);
-    d["nd_lists"] = pair(L.nd_lists);
-    d["nd_counts"] = pair(L.nd_counts);
-    d["nd_nte"] = pair(L.nd_nte);
-    d["nc_rows"] = pair(L.nc_rows);
-    d["nc_w"] = pair(L.nc_w);
-    d["nc_send"] = pair(L.nc_send);
-    d["nc_send_w"] = pair(L.nc_send_w);
-    d["nc_send_off"] = pair(L.nc_send_off);
+    d["inbox_stride"] = L.inbox_stride;
+    d["inbox"] = L.inbox;
+    d["nd_nte"] = L.nd_nte;
+    d["nd_rcnt"] = L.nd_rcnt;
+    d["info"] = L.info;
+    d["prog"] = L.prog;
+    d["max_grid"] = kMaxGrid;
     d["ll_rows"] = pair(L.ll_rows);
     d["ll_ids"] = pair(L.ll_ids);
     d["lc_rows"] = pair(L.lc_rows);
@@ -68,8 +65,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     return d;
   });
   m.def("layout", &layout);
-  m.def("nd_prepare", &nd_prepare);
-  m.def("nd_pull", &nd_pull);
+  m.def("nd_dispatch", &nd_dispatch);
   m.def("nc_combine", &nc_combine);
   m.def("ll_dispatch_send", &ll_dispatch_send);
   m.def("ll_dispatch_recv", &ll_dispatch_recv);
@@ -92,4 +88,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sf_tiles", &sf_tiles);
   m.def("wait_probe", &wait_probe);
   m.def("fence_cost", &fence_cost);
+  m.def("nvl_bw", &nvl_bw, "raw NVLink engine bandwidth probe (all-to-all pattern)");
 }

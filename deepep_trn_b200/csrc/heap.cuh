@@ -2,11 +2,13 @@
 // peer of the EP group through CUDA IPC. All ranks compute the same offsets
 // from the same HeapConfig, so a region of rank p is reached as base[p] + off.
 //
-// Every staging region is double-buffered on the parity of its op's epoch,
-// which removes the "peer finished reading" round trip: a rank only overwrites
-// slot e&1 at epoch e after it has seen every peer's epoch e-1 signal, and a
-// peer only sends that signal after its epoch e-2 reads were complete (stream
-// order on the peer). The argument holds for each op family separately.
+// Normal mode has one inbox per rank: R blocks of M rows, block s holding the
+// rows source s pushed to this rank (dispatch) or the rows expert rank s sent
+// back (combine). Both ops share it under one op sequence number q: a source
+// writes into a peer's inbox (and its progress / info words) for op q only after
+// that peer reported that it finished reading its inbox for op q - 1, so nothing
+// is double-buffered and nothing is ever reset. Low-latency mode keeps two
+// parities of its own receive areas (its own protocol, no host sync).
 #pragma once
 
 #include <cstdint>
@@ -17,29 +19,34 @@ namespace b200ep {
 
 // Device trace points: the last op of each kind stamps %globaltimer at fixed phases.
 enum TracePoint : int {
-  kTrPrepStart = 0, kTrPrepScanDone, kTrPrepCopiesDone, kTrPrepPeersReady, kTrPrepNotified,
-  kTrPullStart = 8, kTrPullEnd,
-  kTrCombStart = 16, kTrCombPushDone, kTrCombPeersReady, kTrCombEnd,  // push done = rows staged (pull form)
+  // normal dispatch: kernel start, scan done (counts published), peers' counts in, host
+  // notified, CTA 0's pushes done, CTA 0's receives done, kernel end
+  kTrNdStart = 0, kTrNdScanned, kTrNdCounts, kTrNdNotified, kTrNdPushed, kTrNdRecvd, kTrNdEnd,
+  // normal combine: kernel start, CTA 0's pushes done, CTA 0's reduction done, kernel end
+  kTrNcStart = 16, kTrNcPushed, kTrNcReduced, kTrNcEnd,
   kTrLLSendStart = 24, kTrLLSendEnd, kTrLLRecvStart, kTrLLRecvReady, kTrLLRecvEnd,
   kTrLCSendStart = 32, kTrLCSendEnd, kTrLCRecvStart, kTrLCRecvReady, kTrLCRecvEnd,
   kTracePoints = 40,
 };
 
 enum EpochId : int {
-  kEpND = 0,    // normal dispatch (prepare kernel advances it)
-  kEpNC = 1,    // normal combine
-  kEpLLD = 2,   // low-latency dispatch (send kernel advances it)
-  kEpLLC = 3,   // low-latency combine (send kernel advances it)
-  kEpBar = 4,   // device barrier
+  kEpInbox = 0,   // normal-mode op sequence (dispatch and combine share the inbox)
+  kEpLLD = 2,     // low-latency dispatch (send kernel advances it)
+  kEpLLC = 3,     // low-latency combine (send kernel advances it)
+  kEpBar = 4,     // device barrier
   kArLLRecv = 5,  // arrival counter of the low-latency dispatch receive kernel
   kArLCRecv = 6,  // arrival counter of the low-latency combine receive kernel
   kNumEpochs = 8,
 };
 
+// Largest CTA count of a normal-mode kernel (one CTA per SM on B200: 148).
+constexpr int kMaxGrid = 256;
+
 // Written by peers (remote stores), polled locally.
 struct Signals {
-  uint32_t nd_ready[2][B200EP_MAX_RANKS];   // source s staged its dispatch data for epoch e
-  uint32_t nc_ready[2][B200EP_MAX_RANKS];   // rank r delivered all its combine rows for epoch e
+  uint64_t nd_cnt[B200EP_MAX_RANKS];    // (q << 32) | rows source s sends this rank
+  uint64_t nd_grid[B200EP_MAX_RANKS];   // (q << 32) | CTAs of source s's dispatch kernel
+  uint32_t inbox_free[B200EP_MAX_RANKS];  // peer p finished reading its own inbox for op q
   uint64_t ll_hdr[2][B200EP_MAX_RANKS];     // (epoch << 32) | num_tokens of source s
   uint32_t ll_cnt[2][B200EP_MAX_RANKS];     // cumulative token slots source s has written (per parity)
   uint32_t lc_cnt[2][B200EP_MAX_RANKS];     // cumulative combine rows rank r has written home
@@ -51,11 +58,11 @@ struct Signals {
 struct LocalState {
   uint32_t epoch[kNumEpochs];
   uint32_t arrive[kNumEpochs];   // grid-completion counters (reset by the last CTA)
-  int64_t nd_recv_off[2][B200EP_MAX_RANKS + 1];   // exclusive prefix of rows per source
-  int64_t nd_num_recv[2];
   uint32_t ll_expect[2][B200EP_MAX_RANKS];        // ll_cnt values already consumed
   uint32_t lc_expect[2][B200EP_MAX_RANKS];        // lc_cnt values already consumed
   uint32_t arrive2[kNumEpochs];                   // second arrival counters (phase ends)
+  uint32_t gbar_count;                            // grid barrier of the normal-mode kernels
+  uint32_t gbar_gen;
   uint64_t trace[kTracePoints];                   // %globaltimer stamps of the last op of each kind
 };
 
@@ -70,13 +77,13 @@ struct HeapConfig {
 
 struct HeapLayout {
   int64_t sig, local;
-  int64_t row_stride;      // bytes per staged row: align16(2H); fp8 rows use [H payload | H/32 scales]
-  // normal dispatch staging (x2)
-  int64_t nd_x[2], nd_topk[2], nd_w[2], nd_lists[2], nd_counts[2], nd_nte[2];
-  // normal combine receive (x2): [R][M] rows of 2H bytes, [R][M][K] weights (push form)
-  int64_t nc_rows[2], nc_w[2];
-  // normal combine send (x2, pull form): [R*M] rows of 2H bytes, [R*M][K] weights, [R+1] offsets
-  int64_t nc_send[2], nc_send_w[2], nc_send_off[2];
+  int64_t row_stride;      // bytes per low-latency row: align16(2H); fp8 rows use [H payload | H/32 scales]
+  int64_t inbox_stride;    // bytes per inbox row: payload, scales, top-k ids and weights, source token
+  int64_t inbox;           // [R][M] rows of inbox_stride bytes
+  int64_t nd_nte;          // [E] int32: this rank's tokens per expert (read by peers)
+  int64_t nd_rcnt;         // [kMaxGrid][R] int32: rows of each CTA's token range per destination
+  int64_t info;            // [R][kMaxGrid][2] uint64: (q << 32) | first row, (q << 32) | rows of (source, CTA)
+  int64_t prog;            // [R][kMaxGrid] uint64: (q << 32) | rows (source, CTA) has pushed here
   // low-latency dispatch receive (x2): [R][Mll] rows, [R][Mll][K] ids
   int64_t ll_rows[2], ll_ids[2];
   // low-latency combine receive (x2): [Mll][K] rows of 2H bytes
@@ -85,6 +92,10 @@ struct HeapLayout {
 };
 
 __host__ __device__ inline int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+// Inbox row: [payload: 2H (16-bit) or H (fp8) | fp8 scales: H/32 | ids: 4K | weights: 4K | token: 4]
+// for dispatch, [payload: 2H | weights: 4K] for combine; the 16-bit dispatch row is the longest.
+__host__ __device__ inline int64_t inbox_row_bytes(int64_t H, int64_t K) { return align_up(2 * H + 8 * K + 4, 16); }
 
 // Every region is followed by a 256-byte guard zone that the host fills with kCanaryByte at
 // construction and checks on request (SymmHeap::check_canaries): a kernel that writes past
@@ -107,23 +118,12 @@ inline HeapLayout make_layout(const HeapConfig& c, int64_t* guards = nullptr, in
   L.sig = take(sizeof(Signals));
   L.local = take(sizeof(LocalState));
   L.row_stride = align_up(2LL * c.H, 16);
-  for (int b = 0; b < 2; ++b) {
-    L.nd_x[b] = take(int64_t(c.M) * L.row_stride);
-    L.nd_topk[b] = take(int64_t(c.M) * c.K * 4);
-    L.nd_w[b] = take(int64_t(c.M) * c.K * 4);
-    L.nd_lists[b] = take(int64_t(c.R) * c.M * 4);
-    L.nd_counts[b] = take(int64_t(c.R) * 4);
-    L.nd_nte[b] = take(int64_t(c.E) * 4);
-  }
-  for (int b = 0; b < 2; ++b) {
-    L.nc_rows[b] = take(int64_t(c.R) * c.M * 2LL * c.H);
-    L.nc_w[b] = take(int64_t(c.R) * c.M * c.K * 4);
-  }
-  for (int b = 0; b < 2; ++b) {
-    L.nc_send[b] = take(int64_t(c.R) * c.M * 2LL * c.H);
-    L.nc_send_w[b] = take(int64_t(c.R) * c.M * c.K * 4);
-    L.nc_send_off[b] = take(int64_t(c.R + 1) * 8);
-  }
+  L.inbox_stride = inbox_row_bytes(c.H, c.K);
+  L.inbox = take(int64_t(c.R) * c.M * L.inbox_stride);
+  L.nd_nte = take(int64_t(c.E) * 4);
+  L.nd_rcnt = take(int64_t(kMaxGrid) * c.R * 4);
+  L.info = take(int64_t(c.R) * kMaxGrid * 16);
+  L.prog = take(int64_t(c.R) * kMaxGrid * 8);
   for (int b = 0; b < 2; ++b) {
     L.ll_rows[b] = take(int64_t(c.R) * c.Mll * L.row_stride);
     L.ll_ids[b] = take(int64_t(c.R) * c.Mll * c.K * 4);

@@ -131,7 +131,10 @@ std::mutex g_scratch_mu;
 
 // Device address of the scratch array on the current device, looked up once per device.
 // In host code the symbol is only a host-side handle; the kernel needs this address.
-cudaError_t scratch_for_current_device(int32_t** out) {
+// The first call on a device also clears the array with an asynchronous memset on the
+// caller's stream, so the clearing is ordered before that call's kernel on the same
+// stream (the array is zero at module load as well, and every launch leaves it at zero).
+cudaError_t scratch_for_current_device(cudaStream_t stream, int32_t** out) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
@@ -141,8 +144,7 @@ cudaError_t scratch_for_current_device(int32_t** out) {
     void* p = nullptr;
     err = cudaGetSymbolAddress(&p, g_layout_scratch);
     if (err != cudaSuccess) return err;
-    // the accumulators must start at zero; every launch leaves them at zero again
-    err = cudaMemset(p, 0, sizeof(g_layout_scratch));
+    err = cudaMemsetAsync(p, 0, sizeof(g_layout_scratch), stream);
     if (err != cudaSuccess) return err;
     g_scratch_ptr[dev] = static_cast<int32_t*>(p);
   }
@@ -167,7 +169,7 @@ extern "C" int b200ep_dispatch_layout_noalloc(const int64_t* topk_idx, int num_t
     return B200EP_NOALLOC_TOO_LARGE;
   }
   int32_t* scratch = nullptr;
-  cudaError_t err = scratch_for_current_device(&scratch);
+  cudaError_t err = scratch_for_current_device(stream, &scratch);
   if (err != cudaSuccess) return static_cast<int>(err);
   const int grid = num_tokens > 0 ? (num_tokens + kLayoutThreads - 1) / kLayoutThreads : 1;
   layout_kernel<int64_t><<<grid, kLayoutThreads, 0, stream>>>(topk_idx, num_tokens, topk, num_experts, num_ranks,

@@ -30,9 +30,10 @@
 // last call; the kernel returns it to zero before it finishes, so calls that run
 // one after another on the GPU are correct, but calls that overlap on the GPU
 // (different streams without ordering between them) race on it and must be avoided.
-// The first call on each device looks up the array's device address and zeroes the
-// array (once, with that device current, synchronously); make that first call before
-// any CUDA stream capture.
+// The first call on each device looks up the array's device address (with that device
+// current) and clears the array with an asynchronous memset on the caller's stream, so
+// the clearing is ordered before that call's kernel; make that first call before any
+// CUDA stream capture.
 // No call allocates or frees memory.
 #pragma once
 

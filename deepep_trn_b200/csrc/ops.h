@@ -31,6 +31,9 @@ class SymmHeap {
   std::vector<int64_t> wait_notify(uint64_t ticket, int num_local_experts, double timeout_s) const;
   // Offsets (bytes into this rank's heap) of the guard zones whose canary bytes changed.
   std::vector<int64_t> check_canaries() const;
+  // Zero the grid-barrier and arrival counters of this rank's local state (after a device
+  // error left a kernel part-way; epochs and sequence numbers are kept).
+  void reset_counters();
 
   int rank() const { return rank_; }
   int world() const { return world_; }
@@ -65,15 +68,15 @@ void layout(const at::Tensor& topk_idx, int64_t num_experts, int64_t num_ranks, 
             at::Tensor itr, at::Tensor scratch);
 
 // normal.cu
-void nd_prepare(SymmHeap& heap, const at::Tensor& x, const OptTensor& x_scales, int64_t mode, bool round_scale,
-                const OptTensor& topk_idx, const OptTensor& topk_w, const OptTensor& nte, const at::Tensor& in_rank,
-                at::Tensor token_pos, at::Tensor recv_off, int64_t num_experts, int64_t ticket, int64_t num_sms);
-void nd_pull(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_scales, const OptTensor& recv_topk,
-             const OptTensor& recv_w, at::Tensor recv_src, int64_t mode, int64_t num_experts, int64_t num_sms,
-             bool use_tma, const OptTensor& local_x, const OptTensor& local_scales);
+void nd_dispatch(SymmHeap& heap, const at::Tensor& x, const OptTensor& x_scales, int64_t mode, bool round_scale,
+                 const OptTensor& topk_idx, const OptTensor& topk_w, const OptTensor& nte, const at::Tensor& in_rank,
+                 at::Tensor token_pos, at::Tensor send_start, at::Tensor recv_info, at::Tensor recv_off,
+                 at::Tensor recv_x, const OptTensor& recv_scales, const OptTensor& recv_topk,
+                 const OptTensor& recv_w, at::Tensor recv_src, int64_t num_experts, int64_t ticket, int64_t grid,
+                 bool pad_rows);
 void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const at::Tensor& recv_off,
-                const at::Tensor& token_pos, at::Tensor out, const OptTensor& out_w, const OptTensor& bias0,
-                const OptTensor& bias1, int64_t num_sms);
+                const at::Tensor& recv_info, const at::Tensor& token_pos, const at::Tensor& send_start, at::Tensor out,
+                const OptTensor& out_w, const OptTensor& bias0, const OptTensor& bias1, int64_t grid);
 
 // ll.cu
 void ll_dispatch_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& topk_idx, int64_t num_experts,
@@ -90,6 +93,10 @@ void ll_combine_recv(SymmHeap& heap, const at::Tensor& topk_idx, const at::Tenso
 void device_barrier(SymmHeap& heap);
 void wait_probe(SymmHeap& heap, int64_t budget_ns);
 void fence_cost(SymmHeap& heap, int64_t peer, int64_t bytes, int64_t scope, at::Tensor out);
+
+// nvlbench.cu
+void nvl_bw(SymmHeap& heap, int64_t mode, int64_t bytes_per_peer, int64_t chunk, int64_t nstages, int64_t grid,
+            int64_t threads);
 
 // gemm.cu
 void grouped_gemm_m(const at::Tensor& A, const at::Tensor& B, const at::Tensor& offsets, const OptTensor& C,

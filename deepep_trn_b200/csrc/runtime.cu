@@ -138,12 +138,25 @@ std::vector<int64_t> SymmHeap::wait_notify(uint64_t ticket, int num_local_expert
     }
   }
   std::atomic_thread_fence(std::memory_order_acquire);
+  // the kernel publishes the ticket even after a failed wait (with a zero size): report it
+  if (s->code != 0) throw std::runtime_error("device error during dispatch (code " + std::to_string(s->code) + ")");
   std::vector<int64_t> out;
   out.reserve(1 + world_ + num_local_experts);
   out.push_back(static_cast<int64_t>(n->num_recv));
   for (int r = 0; r < world_; ++r) out.push_back(static_cast<int64_t>(n->recv_counts[r]));
   for (int e = 0; e < num_local_experts && e < 1024; ++e) out.push_back(static_cast<int64_t>(n->per_expert[e]));
   return out;
+}
+
+void SymmHeap::reset_counters() {
+  if (local_ == nullptr) return;
+  B200EP_CUDA_CHECK(cudaSetDevice(device_));
+  B200EP_CUDA_CHECK(cudaDeviceSynchronize());
+  uint8_t* ls = static_cast<uint8_t*>(local_) + layout_.local;
+  B200EP_CUDA_CHECK(cudaMemset(ls + offsetof(LocalState, arrive), 0, sizeof(LocalState::arrive)));
+  B200EP_CUDA_CHECK(cudaMemset(ls + offsetof(LocalState, arrive2), 0, sizeof(LocalState::arrive2)));
+  B200EP_CUDA_CHECK(cudaMemset(ls + offsetof(LocalState, gbar_count), 0, sizeof(uint32_t)));
+  B200EP_CUDA_CHECK(cudaDeviceSynchronize());
 }
 
 std::vector<int64_t> SymmHeap::check_canaries() const {

@@ -3,11 +3,12 @@
 One op = one or two kernel launches on the caller's stream:
 
   get_dispatch_layout  -> layout kernel (N1), no host round trip
-  dispatch             -> nd_prepare (stage / quantise / scan / count exchange),
-                          host waits on a host-mapped ticket for the receive size
-                          (skipped for a cached dispatch or with num_worst_tokens),
-                          nd_pull (receivers pull their rows with TMA bulk copies)
-  combine              -> nc_combine (push home + fp32 reduce, one cooperative kernel)
+  dispatch             -> nd_dispatch (one cooperative kernel: scan, count exchange, push
+                          rows into the peers' inboxes, copy received rows out); the host
+                          waits on a host-mapped ticket for the receive size while the
+                          kernel is still moving rows (skipped for a cached dispatch or
+                          with num_worst_tokens)
+  combine              -> nc_combine (one cooperative kernel: push rows home, fp32 reduce)
   low_latency_dispatch -> ll_dispatch_send [+ ll_dispatch_recv, or via the hook]
   low_latency_combine  -> ll_combine_send  [+ ll_combine_recv, or via the hook]
 
@@ -16,7 +17,6 @@ heap exists (call them once before capture).
 """
 from __future__ import annotations
 
-import os
 
 import torch
 import torch.distributed as dist
@@ -55,6 +55,7 @@ class NvlinkEngine:
         self.last_exchange = None
         self._last_spec = None
         self._spec_cache: dict = {}
+        self.max_grid = int(self.C.heap_layout(1, 1, 1, 8, 1, 1)['max_grid'])
         if spec_hint is not None:
             self._ensure(spec_hint)
 
@@ -79,6 +80,9 @@ class NvlinkEngine:
         code, op, rank, peer, expected, seen, aux = self.heap.status()
         if code:
             self.heap.clear_status()
+            # a kernel that gave up part-way leaves its grid counters behind: zero them so
+            # the buffer stays usable for the next op
+            self.heap.reset_counters()
             raise DeviceError(f'{ERRORS.get(code, "device error")} (code={code} op={op} rank={rank} '
                               f'peer={peer} expected={expected} seen={seen} aux={aux})')
 
@@ -100,11 +104,11 @@ class NvlinkEngine:
 
         def d(a, b):
             return round((t[b] - t[a]) / 1e3, 2) if t[a] and t[b] else None
-        return {'prepare.scan': d(0, 1), 'prepare.copies': d(0, 2), 'prepare.wait_peers': d(2, 3),
-                'prepare.notify': d(3, 4), 'prepare.total': d(0, 4), 'gap.prepare_to_pull': d(4, 8),
-                'pull': d(8, 9), 'gap.pull_to_combine': d(9, 16), 'combine.push': d(16, 17),
-                'combine.wait_peers': d(17, 18), 'combine.reduce': d(18, 19), 'combine.total': d(16, 19),
-                'step.prepare_to_combine_end': d(0, 19)}
+        return {'dispatch.scan': d(0, 1), 'dispatch.counts_in': d(0, 2), 'dispatch.notified': d(0, 3),
+                'dispatch.cta0_pushed': d(0, 4), 'dispatch.cta0_received': d(0, 5), 'dispatch.total': d(0, 6),
+                'gap.dispatch_to_combine': d(6, 16), 'combine.cta0_pushed': d(16, 17),
+                'combine.cta0_reduced': d(16, 18), 'combine.total': d(16, 19),
+                'step.dispatch_to_combine_end': d(0, 19)}
 
     def barrier(self) -> None:
         """Device-side barrier over the EP group (epoch flags in peer memory, bounded wait)."""
@@ -131,6 +135,11 @@ class NvlinkEngine:
         from ..buffer import Buffer
         n = getattr(config, 'num_sms', 0) if config is not None else 0
         return int(n or Buffer.num_sms or 0)
+
+    def _grid(self, config) -> int:
+        """CTAs of the normal-mode kernels (one per SM by default); every rank must use the same."""
+        n = self._sms(config)
+        return max(1, min(int(n) if n else self.heap.num_sms, self.max_grid))
 
     def _spec(self, H, K, E, Mll=None) -> HeapSpec:
         key = (H, K, E, Mll)
@@ -182,27 +191,23 @@ class NvlinkEngine:
         EL = experts_per_rank(E, self.R)
         self._ensure(self._spec(H, K, E))
         mode = 1 if fp8_in else (2 if use_fp8 else 0)
-        token_pos = torch.empty(T, self.R, dtype=torch.int32, device=dev)
-        recv_off = torch.empty(self.R + 1, dtype=torch.int64, device=dev)
+        R = self.R
+        G = self._grid(config)
+        token_pos = torch.empty(T, R, dtype=torch.int32, device=dev)
+        send_start = torch.empty(G, R, dtype=torch.int32, device=dev)
+        recv_info = torch.empty(R, self.max_grid, 2, dtype=torch.int32, device=dev)
+        recv_off = torch.empty(R + 1, dtype=torch.int64, device=dev)
         self.ticket += 1
-        nsm = self._sms(config)
-        x_scales = x[1].float().contiguous() if fp8_in else None
-        with timer.stage('prepare'):
-            self.C.nd_prepare(self.heap, xt if not fp8_in else xt.view(torch.uint8),
-                              x_scales, mode, bool(round_scale),
-                              None if cached else _contig(topk_idx),
-                              None if (cached or topk_weights is None) else _contig(_f32(topk_weights)),
-                              None if cached else _contig(nte if nte.dtype == torch.int32 else nte.to(torch.int32)),
-                              _contig(itr), token_pos, recv_off, E, self.ticket, nsm)
-        # Outputs are sized for the worst case (every peer sends its full capacity) so the pull
-        # kernel can be queued before the host learns the receive size; the host then waits
-        # on the notify ticket while the GPU is already pulling, and returns the first N rows.
+        x_scales = x[1].float() if fp8_in else None
+        # Outputs are sized for the worst case (every peer sends its full capacity) so the kernel
+        # is queued before the host learns the receive size; the host then waits on the notify
+        # ticket while the GPU is still moving rows, and returns the first N rows.
         if num_worst_tokens:
             cap = int(num_worst_tokens)
         elif cached:
             cap = handle.num_recv if handle.num_recv is not None else handle.capacity
         else:
-            cap = self.R * self.M
+            cap = R * self.M
         if mode == 0:
             recv_x = torch.empty(cap, H, dtype=xt.dtype, device=dev)
             recv_s = None
@@ -215,13 +220,15 @@ class NvlinkEngine:
             if topk_weights is not None:
                 recv_w = torch.empty(cap, K, dtype=torch.float32, device=dev)
         recv_src = torch.empty(cap, dtype=torch.int64, device=dev)
-        use_tma = True if config is None else bool(getattr(config, 'use_tma', True))
-        if os.environ.get('B200EP_NO_TMA'):
-            use_tma = False
-        with timer.stage('pull'):
-            self.C.nd_pull(self.heap, recv_x, recv_s, recv_topk, recv_w, recv_src, mode, E, nsm, use_tma,
-                           xt if mode == 0 else (xt.view(torch.uint8) if mode == 1 else None),
-                           x_scales)
+        with timer.stage('dispatch'):
+            self.C.nd_dispatch(self.heap, xt if not fp8_in else xt.view(torch.uint8), x_scales, mode,
+                               bool(round_scale),
+                               None if cached else _contig(topk_idx),
+                               None if (cached or topk_weights is None) else _contig(_f32(topk_weights)),
+                               None if cached else _contig(nte if nte.dtype == torch.int32 else nte.to(torch.int32)),
+                               _contig(itr), token_pos, send_start, recv_info, recv_off,
+                               recv_x, recv_s, recv_topk, recv_w, recv_src, E, self.ticket, G,
+                               bool(num_worst_tokens))
         per_expert = recv_counts = None
         if num_worst_tokens or cached:
             N = cap
@@ -231,14 +238,14 @@ class NvlinkEngine:
                 try:
                     info = self.heap.wait_notify(self.ticket, EL, self.host_timeout_s)
                 except RuntimeError:
-                    # every wait of the queued kernels is bounded: let them finish so nothing of
+                    # every wait of the queued kernel is bounded: let it finish so nothing of
                     # this op is in flight, then raise with the device's own record
                     torch.cuda.synchronize()
                     self.check()
                     raise
             N = int(info[0])
-            recv_counts = torch.tensor(info[1:1 + self.R], dtype=torch.int64)
-            per_expert = info[1 + self.R:1 + self.R + EL]
+            recv_counts = torch.tensor(info[1:1 + R], dtype=torch.int64)
+            per_expert = info[1 + R:1 + R + EL]
             if expert_alignment > 1:
                 per_expert = [(c + expert_alignment - 1) // expert_alignment * expert_alignment for c in per_expert]
             recv_x, recv_src = recv_x[:N], recv_src[:N]
@@ -248,6 +255,7 @@ class NvlinkEngine:
         new = DispatchHandle(T, K, None, recv_counts, recv_src, itr, num_recv=None if num_worst_tokens else N,
                              token_pos=token_pos, recv_off=recv_off, hidden=H, num_experts=E)
         new.capacity = cap
+        new.send_start, new.recv_info, new.grid = send_start, recv_info, G
         self.last_exchange = dict(mode='normal', rows=N, hidden=H, payload_bytes=(2 * H if mode == 0 else H + H // 32))
         out_x = recv_x if mode == 0 else (recv_x, recv_s)
         if cached:
@@ -270,11 +278,12 @@ class NvlinkEngine:
         out_w = torch.empty(T, topk_weights.shape[1], dtype=torch.float32, device=x.device) \
             if topk_weights is not None else None
         b = [t.contiguous() for t in bias]
+        xc = x if (x.stride(1) == 1 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0) else x.contiguous()
         with timer.stage('combine'):
-            self.C.nc_combine(self.heap, x if x.stride(1) == 1 else x.contiguous(),
+            self.C.nc_combine(self.heap, xc,
                               _contig(_f32(topk_weights)) if topk_weights is not None else None,
-                              handle.recv_off, handle.token_pos, out, out_w,
-                              b[0] if len(b) > 0 else None, b[1] if len(b) > 1 else None, self._sms(config))
+                              handle.recv_off, handle.recv_info, handle.token_pos, handle.send_start, out, out_w,
+                              b[0] if len(b) > 0 else None, b[1] if len(b) > 1 else None, handle.grid)
         if out_w is not None and topk_weights.dtype != torch.float32:
             out_w = out_w.to(topk_weights.dtype)
         return out, out_w, EventOverlap()

@@ -11,7 +11,7 @@ singleton ``timer``. Two additions for the GPU:
 * every stage is also an NVTX range (``torch.cuda.nvtx``) when CUDA is present, so
   the stages line up with kernels in a profiler timeline.
 
-Stage names used by the Buffer: ``layout, prepare, notify_wait, alloc, pull, combine,
+Stage names used by the Buffer: ``layout, dispatch, notify_wait, combine,
 ll_send, ll_recv`` for the NVLink engine and the reference's ``in_d2h, plan, pack,
 h2d, kernel, d2h, unpack, out_h2d`` for the transport engines.
 """

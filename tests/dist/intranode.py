@@ -1,124 +1,166 @@
-"""Normal-mode dispatch / combine against an all-gather oracle.
+"""Normal-mode dispatch / combine of every rank checked against an oracle built from the
+whole EP group's inputs (gathered over a gloo group, so independent of the path under test).
 
 torchrun --nnodes 1 --nproc-per-node 4 --master-addr 127.0.0.1 tests/dist/intranode.py --backend gloo --ep 2
-(reference scenario: tests/dist/test_intranode.py of deep_ep_trn)
+
+Scenarios (the same list as deep_ep_trn's tests/dist/test_intranode.py, plus the API paths
+the reference leaves unimplemented): layout, dispatch rows / ids / weights / sources /
+per-expert counts, cached dispatch, identity and emulated-expert combine, combine weights,
+bias, fp8 (in-kernel quantisation and pre-quantised tuples), expert_alignment,
+num_worst_tokens (also under CUDA-graph capture), async_finish / previous_event /
+allocate_on_comm_stream, and the same op on several grid sizes (NVLink backend).
 """
-from common import (bitwise_equal, device, expert_scale, finish, gather_peers, init, make_buffer, make_routing,
-                    parse_args)
+from __future__ import annotations
+
+from harness import Scenario
 
 import torch
 
 from deepep_trn_b200.utils.codec import quantize_fp8_1x128
-from deepep_trn_b200.utils.layout import rank_of_expert
+from deepep_trn_b200.utils.layout import get_dispatch_layout, rank_of_expert
+from deepep_trn_b200.utils.testing import bitwise_equal, expert_scale, make_routing
 
 
-def naive_layout(idx, experts, ep):
-    local = experts // ep
-    in_rank = torch.zeros(idx.shape[0], ep, dtype=torch.bool)
-    per_expert = torch.zeros(experts, dtype=torch.int64)
-    for t in range(idx.shape[0]):
-        for e in idx[t].tolist():
-            if e >= 0:
-                in_rank[t, e // local] = True
-                per_expert[e] += 1
-    return in_rank.sum(0), per_expert, in_rank
+def oracle(shared, me: int, R: int, E: int):
+    """What rank ``me`` must receive: for every source in group order, the source's tokens
+    that have at least one expert on ``me`` (in token order), their ids mapped to local
+    experts (-1 elsewhere), their weights (0 elsewhere) and their source token index."""
+    EL = E // R
+    parts = {'x': [], 'idx': [], 'w': [], 'src': []}
+    for x, idx, w in shared:
+        mine = rank_of_expert(idx, E, R) == me
+        keep = mine.any(1)
+        parts['x'].append(x[keep])
+        parts['idx'].append(torch.where(mine[keep], idx[keep] - me * EL, -1))
+        parts['w'].append(torch.where(mine[keep], w[keep], 0.0))
+        parts['src'].append(keep.nonzero().flatten())
+    return {k: torch.cat(v) for k, v in parts.items()}
+
+
+def layout_args(buf, d_idx, E):
+    ntr, _, nte, itr, _ = buf.get_dispatch_layout(d_idx, E)
+    return dict(topk_idx=d_idx, num_tokens_per_rank=ntr, is_token_in_rank=itr, num_tokens_per_expert=nte), itr
 
 
 def main():
-    args = parse_args(__doc__)
-    rank, world, control = init(args.backend)
-    buf, peers = make_buffer(args.backend, args.ep, args.max_tokens)
-    dev = device(args.backend)
-    R, E, K, H = buf.group_size, args.experts, args.topk, args.hidden
-    EL, me = E // R, buf.rank
-    lo = me * EL
-    for kind in args.kinds.split(','):
-        idx, w = make_routing(kind, args.tokens, E, K, R, me, seed=1000 + rank)
+    sc = Scenario(__doc__)
+    a = sc.args
+    buf = sc.buffer()
+    R, E, K, H = buf.group_size, a.experts, a.topk, a.hidden
+    me, EL = buf.rank, a.experts // buf.group_size
+    nvlink = sc.backend == 'nvlink'
+    for kind in a.kinds.split(','):
+        idx, w = make_routing(kind, a.tokens, E, K, R, me, seed=1000 + sc.rank)
         T = idx.shape[0]
-        x = torch.randn(T, H, generator=torch.Generator().manual_seed(rank)).to(torch.bfloat16)
-        d_x, d_idx, d_w = x.to(dev), idx.to(dev), w.to(dev)
+        x = torch.randn(T, H, generator=torch.Generator().manual_seed(sc.rank)).to(torch.bfloat16)
+        d_x, d_idx, d_w = sc.dev(x), sc.dev(idx), sc.dev(w)
+        exp = oracle(sc.share((x, idx, w)), me, R, E)
+        visits = get_dispatch_layout(idx, E, R)[2].sum(1, keepdim=True)
 
-        ntr, _, nte, itr, _ = buf.get_dispatch_layout(d_idx, E)
-        ref_ntr, ref_nte, ref_itr = naive_layout(idx, E, R)
-        assert torch.equal(ntr.cpu().long(), ref_ntr) and torch.equal(nte.cpu().long(), ref_nte), (kind, 'layout')
-        assert torch.equal(itr.cpu(), ref_itr), (kind, 'is_token_in_rank')
+        # ---- layout on the device equals the torch definition
+        kw, itr = layout_args(buf, d_idx, E)
+        ref_ntr, ref_nte, ref_itr = get_dispatch_layout(idx, E, R)
+        assert torch.equal(sc.host(kw['num_tokens_per_rank']).long(), ref_ntr.long()), (kind, 'tokens per rank')
+        assert torch.equal(sc.host(kw['num_tokens_per_expert']).long(), ref_nte.long()), (kind, 'tokens per expert')
+        assert torch.equal(sc.host(itr), ref_itr), (kind, 'is_token_in_rank')
 
-        recv_x, recv_idx, recv_w, per_expert, handle, _ = buf.dispatch(
-            d_x, topk_idx=d_idx, topk_weights=d_w, num_tokens_per_rank=ntr, is_token_in_rank=itr,
-            num_tokens_per_expert=nte)
-        recv_x, recv_idx, recv_w = recv_x.cpu(), recv_idx.cpu(), recv_w.cpu()
+        # ---- dispatch
+        rx, ridx, rw, per_expert, handle, _ = buf.dispatch(d_x, topk_weights=d_w, **kw)
+        rx, ridx, rw = sc.host(rx), sc.host(ridx), sc.host(rw)
+        assert bitwise_equal(rx, exp['x']), (kind, 'recv_x')
+        assert torch.equal(ridx, exp['idx']) and torch.equal(rw, exp['w']), (kind, 'recv ids / weights')
+        assert torch.equal(sc.host(handle.recv_src_idx).long(), exp['src']), (kind, 'recv_src_idx')
+        want = torch.bincount(exp['idx'][exp['idx'] >= 0], minlength=EL)
+        assert per_expert == want.tolist(), (kind, 'per-expert counts')
+        again, *_ = buf.dispatch(d_x, handle=handle)
+        assert bitwise_equal(sc.host(again), rx), (kind, 'cached dispatch')
 
-        exp_x, exp_idx, exp_w, exp_src = [], [], [], []
-        for px, pidx, pw in gather_peers((x, idx, w), peers, control):
-            owner = rank_of_expert(pidx, E, R)
-            rows = (owner == me).any(1).nonzero().flatten()
-            local = owner[rows] == me
-            exp_x.append(px[rows])
-            exp_src.append(rows)
-            exp_idx.append(torch.where(local, pidx[rows] - lo, torch.full_like(pidx[rows], -1)))
-            exp_w.append(torch.where(local, pw[rows], torch.zeros_like(pw[rows])))
-        exp_x, exp_idx, exp_w, exp_src = (torch.cat(v) for v in (exp_x, exp_idx, exp_w, exp_src))
-        assert bitwise_equal(recv_x, exp_x), (kind, 'recv_x')
-        assert torch.equal(recv_idx, exp_idx), (kind, 'recv_topk_idx')
-        assert torch.equal(recv_w, exp_w), (kind, 'recv_topk_weights')
-        assert torch.equal(handle.recv_src_idx.cpu().long(), exp_src), (kind, 'recv_src_idx')
-        assert per_expert == torch.bincount(exp_idx[exp_idx >= 0], minlength=EL).tolist(), (kind, 'per_expert')
-
-        cached_x, *_ = buf.dispatch(d_x, handle=handle)
-        assert bitwise_equal(cached_x.cpu(), recv_x), (kind, 'cached dispatch')
-
-        # identity combine: each token comes back once per rank it visited
-        combined, combined_w, _ = buf.combine(recv_x.to(dev), handle, topk_weights=recv_w.to(dev))
-        ref = (x.float() * ref_itr.sum(1, keepdim=True)).to(torch.bfloat16)
-        assert torch.equal(combined.cpu(), ref), (kind, 'identity combine')
-        assert torch.equal(combined_w.cpu(), torch.where(idx >= 0, w, torch.zeros_like(w))), (kind, 'weights')
-
-        # emulated experts: the receiver reduces its local experts per row, combine sums ranks
-        coef = (expert_scale(recv_idx + lo) * recv_w * (recv_idx >= 0)).sum(-1, keepdim=True)
-        y = (recv_x.float() * coef).to(torch.bfloat16)
-        combined, _, _ = buf.combine(y.to(dev), handle)
+        # ---- combine: identity, weights, emulated experts, bias
+        ident = (x.float() * visits).to(torch.bfloat16)
+        out, out_w, _ = buf.combine(sc.dev(rx), handle, topk_weights=sc.dev(rw))
+        assert torch.equal(sc.host(out), ident), (kind, 'identity combine')
+        assert torch.equal(sc.host(out_w), torch.where(idx >= 0, w, 0.0)), (kind, 'combined weights')
+        gain = (expert_scale(ridx + me * EL) * rw * (ridx >= 0)).sum(-1, keepdim=True)
+        out, _, _ = buf.combine(sc.dev((rx.float() * gain).to(torch.bfloat16)), handle)
         ref = x.float() * (expert_scale(idx) * w * (idx >= 0)).sum(-1, keepdim=True)
-        diff = (combined.cpu().float() - ref).abs()
-        rel = float(diff.mean() / ref.abs().mean().clamp_min(1e-9)) if T else 0.0
-        assert torch.allclose(combined.cpu().float(), ref, rtol=2e-2, atol=2e-3) and rel < 1e-2, (kind, rel)
+        got = sc.host(out).float()
+        rel = float((got - ref).abs().mean() / ref.abs().mean().clamp_min(1e-9)) if T else 0.0
+        assert torch.allclose(got, ref, rtol=2e-2, atol=2e-3) and rel < 1e-2, (kind, 'expert combine', rel)
+        bias = torch.randn(T, H, generator=torch.Generator().manual_seed(7 + sc.rank)).to(torch.bfloat16)
+        out, _, _ = buf.combine(sc.dev(rx), handle, bias=sc.dev(bias))
+        assert torch.equal(sc.host(out), (x.float() * visits + bias.float()).to(torch.bfloat16)), (kind, 'bias')
 
-        # combine with bias: added in fp32 before the single cast
-        bias = torch.randn(T, H, generator=torch.Generator().manual_seed(7 + rank)).to(torch.bfloat16)
-        combined, _, _ = buf.combine(recv_x.to(dev), handle, bias=bias.to(dev))
-        ref = (x.float() * ref_itr.sum(1, keepdim=True) + bias.float()).to(torch.bfloat16)
-        assert torch.equal(combined.cpu(), ref), (kind, 'bias combine')
+        # ---- expert_alignment rounds the per-expert counts up
+        *_, per_al, _, _ = buf.dispatch(d_x, expert_alignment=4, **kw)
+        assert per_al == [(c + 3) // 4 * 4 for c in want.tolist()], (kind, 'expert_alignment')
 
-        if args.fp8 and H % 128 == 0:
-            # fp8 in the dispatch kernel: receiver gets q/scales of exactly the oracle rows
-            (rq, rs), *_ = buf.dispatch(d_x, topk_idx=d_idx, topk_weights=d_w, num_tokens_per_rank=ntr,
-                                        is_token_in_rank=itr, num_tokens_per_expert=nte, use_fp8=True)
-            eq, es = quantize_fp8_1x128(exp_x)
-            assert bitwise_equal(rq.cpu(), eq) and torch.equal(rs.cpu(), es), (kind, 'fp8 dispatch')
-            # pre-quantised tuple input passes through bit-exactly
-            q, s = quantize_fp8_1x128(x, round_scale=True)
-            (rq, rs), *_ = buf.dispatch((q.to(dev), s.to(dev)), handle=handle)
-            eq, es = quantize_fp8_1x128(exp_x, round_scale=True)
-            assert bitwise_equal(rq.cpu(), eq) and torch.equal(rs.cpu(), es), (kind, 'fp8 tuple dispatch')
-        if args.backend == 'nvlink' and kind == args.kinds.split(',')[0]:
-            # repeat-and-compare: the same dispatch / combine on 1..all SMs must give the same bits
-            # (an ordering race would show up as a difference between grid sizes)
-            from deepep_trn_b200 import Buffer
-            ident = (x.float() * ref_itr.sum(1, keepdim=True)).to(torch.bfloat16)
-            for n in (1, 3, 7, 16, 61, 0):
-                Buffer.set_num_sms(n)
-                rx2, _, _, _, h2, _ = buf.dispatch(d_x, topk_idx=d_idx, topk_weights=d_w, num_tokens_per_rank=ntr,
-                                                   is_token_in_rank=itr, num_tokens_per_expert=nte)
-                c2, _, _ = buf.combine(rx2, h2)
-                assert bitwise_equal(rx2.cpu(), recv_x), (kind, 'repeat dispatch', n)
-                assert torch.equal(c2.cpu(), ident), (kind, 'repeat combine', n)
-            Buffer.set_num_sms(0)
+        # ---- fp8: quantised inside the dispatch, or passed through as (e4m3, scales)
+        if a.fp8 and H % 128 == 0:
+            (q, s), *_ = buf.dispatch(d_x, topk_weights=d_w, use_fp8=True, **kw)
+            eq, es = quantize_fp8_1x128(exp['x'])
+            assert bitwise_equal(sc.host(q), eq) and torch.equal(sc.host(s), es), (kind, 'fp8 dispatch')
+            pq, ps = quantize_fp8_1x128(x, round_scale=True)
+            (q, s), *_ = buf.dispatch(sc.dev((pq, ps)), handle=handle)
+            eq, es = quantize_fp8_1x128(exp['x'], round_scale=True)
+            assert bitwise_equal(sc.host(q), eq) and torch.equal(sc.host(s), es), (kind, 'fp8 tuple dispatch')
+
+        if nvlink:
+            N = exp['x'].shape[0]
+            cap = R * a.max_tokens
+            # ---- num_worst_tokens: no host sync, rows past N carry no expert, weight 0, source -1
+            wx, widx, ww, _, wh, _ = buf.dispatch(d_x, topk_weights=d_w, num_worst_tokens=cap, **kw)
+            assert wx.shape[0] == cap and widx.shape == (cap, K)
+            assert bitwise_equal(sc.host(wx[:N]), exp['x']) and torch.equal(sc.host(widx[:N]), exp['idx'])
+            assert (sc.host(widx[N:]) == -1).all() and (sc.host(ww[N:]) == 0).all(), (kind, 'padding ids / weights')
+            assert (sc.host(wh.recv_src_idx[N:]) == -1).all(), (kind, 'padding sources')
+            out, _, _ = buf.combine(wx, wh)
+            assert torch.equal(sc.host(out), ident), (kind, 'combine after num_worst_tokens')
+
+            # ---- the same, captured once in a CUDA graph and replayed
+            if a.graph:
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                side = torch.cuda.Stream()
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side), torch.cuda.graph(g, stream=side):
+                    gkw, _ = layout_args(buf, d_idx, E)
+                    gx, _, _, _, gh, _ = buf.dispatch(d_x, topk_weights=d_w, num_worst_tokens=cap, **gkw)
+                    gout, _, _ = buf.combine(gx, gh)
+                torch.cuda.current_stream().wait_stream(side)
+                for _ in range(3):
+                    gout.zero_()
+                    g.replay()
+                    torch.cuda.synchronize()
+                    assert torch.equal(sc.host(gout), ident), (kind, 'graph replay')
+                del g
+
+            # ---- async_finish / previous_event / allocate_on_comm_stream
+            from deepep_trn_b200 import EventOverlap
+            before = torch.cuda.Event()
+            before.record()
+            res = buf.dispatch(d_x, topk_weights=d_w, previous_event=EventOverlap(before), async_finish=True,
+                               allocate_on_comm_stream=True, **kw)
+            res[-1].current_stream_wait()
+            assert bitwise_equal(sc.host(res[0]), exp['x']), (kind, 'async dispatch')
+            out, _, ev = buf.combine(res[0], res[4], async_finish=True)
+            with ev:
+                pass
+            assert torch.equal(sc.host(out), ident), (kind, 'async combine')
+
+            # ---- repeat-and-compare over grid sizes: an ordering race would change the bits
+            if kind == a.kinds.split(',')[0]:
+                from deepep_trn_b200 import Buffer
+                for n in (1, 3, 7, 16, 61, 0):
+                    Buffer.set_num_sms(n)
+                    rx2, _, _, _, h2, _ = buf.dispatch(d_x, topk_weights=d_w, **kw)
+                    c2, _, _ = buf.combine(rx2, h2)
+                    assert bitwise_equal(sc.host(rx2), rx), (kind, 'repeat dispatch', n)
+                    assert torch.equal(sc.host(c2), ident), (kind, 'repeat combine', n)
+                Buffer.set_num_sms(0)
         buf.check()
         buf.check_canaries()
-        print(f'RANK={rank} intranode {kind}: T={T} sent={handle.send_counts.tolist()} '
-              f'recv={handle.recv_counts.tolist()} expert_combine_rel={rel:.2e} PASS', flush=True)
-    finish(control, buf)
-    if rank == 0:
-        print(f'INTRANODE_PASS backend={args.backend} ep={R}', flush=True)
+        sc.log(f'intranode {kind}: T={T} recv={exp["x"].shape[0]} expert_combine_rel={rel:.2e} PASS')
+    sc.done('INTRANODE')
 
 
 if __name__ == '__main__':

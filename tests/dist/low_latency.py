@@ -3,12 +3,12 @@
 torchrun --nnodes 1 --nproc-per-node 4 --master-addr 127.0.0.1 tests/dist/low_latency.py --backend gloo
 (reference scenario: tests/dist/test_low_latency.py of deep_ep_trn)
 """
-from common import (bitwise_equal, device, expert_scale, finish, gather_peers, init, make_buffer, make_routing,
-                    parse_args)
+from harness import Scenario
 
 import torch
 
 from deepep_trn_b200.utils.codec import dequantize_fp8_1x128, quantize_fp8_1x128
+from deepep_trn_b200.utils.testing import bitwise_equal, expert_scale, make_routing
 
 
 def check_layout(kind, recv_x, recv_count, handle, peer_data, lo, EL, R, fp8):
@@ -34,10 +34,10 @@ def check_layout(kind, recv_x, recv_count, handle, peer_data, lo, EL, R, fp8):
 
 
 def main():
-    args = parse_args(__doc__)
-    rank, world, control = init(args.backend)
-    buf, peers = make_buffer(args.backend, args.ep, args.max_tokens)
-    dev = device(args.backend)
+    sc = Scenario(__doc__)
+    args, rank = sc.args, sc.rank
+    buf = sc.buffer()
+    dev = sc.device
     R, E, K, H, M = buf.group_size, args.experts, args.topk, args.hidden, args.max_tokens
     EL, me = E // R, buf.rank
     lo = me * EL
@@ -45,7 +45,7 @@ def main():
         idx, w = make_routing(kind, args.tokens, E, K, R, me, seed=2000 + rank)
         T = idx.shape[0]
         x = torch.randn(T, H, generator=torch.Generator().manual_seed(rank)).to(torch.bfloat16)
-        peer_data = gather_peers((x, idx), peers, control)
+        peer_data = sc.share((x, idx))
         for fp8 in ((False, True) if (args.fp8 and H % 128 == 0) else (False,)):
             hook_mode = bool(i % 2)
             recv_x, recv_count, handle, _, hook = buf.low_latency_dispatch(
@@ -101,9 +101,7 @@ def main():
         buf.check_canaries()
         print(f'RANK={rank} low_latency {kind}: T={T} recv_count_sum={int(rc.sum())} combine_rel={rel:.2e} PASS',
               flush=True)
-    finish(control, buf)
-    if rank == 0:
-        print(f'LOW_LATENCY_PASS backend={args.backend} ep={R}', flush=True)
+    sc.done('LOW_LATENCY')
 
 
 if __name__ == '__main__':

@@ -10,7 +10,7 @@ torchrun --nnodes 1 --nproc-per-node 4 --master-addr 127.0.0.1 tests/dist/ref_pa
 import sys
 from pathlib import Path
 
-from common import KINDS, bitwise_equal, init, make_routing
+from harness import ROUTING_KINDS, Scenario
 
 ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT / 'baseline' / '_ref'))
@@ -18,16 +18,19 @@ sys.path.insert(0, str(ROOT / 'baseline' / '_ref'))
 import torch
 import torch.distributed as dist
 
+from deepep_trn_b200.utils.testing import bitwise_equal, make_routing
+
 
 def main():
     from deep_ep_trn import Buffer as RefBuffer
     from deepep_trn_b200 import Buffer
-    rank, world, control = init('gloo')
+    sc = Scenario(__doc__)
+    rank, world = sc.rank, sc.world
     group = dist.new_group(backend='gloo')
     M, H, E, K = 32, 256, 32, 4
     ref = RefBuffer(group, backend='gloo', num_max_tokens_per_rank=M)
     ours = Buffer(group, backend='gloo', num_max_tokens_per_rank=M)
-    for kind in KINDS:
+    for kind in ROUTING_KINDS.split(','):
         idx, w = make_routing(kind, 24, E, K, world, rank, seed=3000 + rank)
         T = idx.shape[0]
         x = torch.randn(T, H, generator=torch.Generator().manual_seed(rank)).to(torch.bfloat16)
@@ -60,10 +63,7 @@ def main():
         ob = ours.low_latency_combine(y, idx, w, lb[2])[0]
         assert bitwise_equal(oa, ob), (kind, 'll combine')
         print(f'RANK={rank} parity {kind}: T={T} PASS', flush=True)
-    dist.barrier(group=control)
-    if rank == 0:
-        print('REF_PARITY_PASS', flush=True)
-    dist.destroy_process_group()
+    sc.done('REF_PARITY')
 
 
 if __name__ == '__main__':

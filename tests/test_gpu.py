@@ -102,7 +102,7 @@ def test_intranode_nvlink(run_dist, hidden, experts, topk, tokens, maxt):
     n = _ngpus()
     nproc = n if n in (1, 2, 4, 8) else 1
     rc, out = run_dist('intranode.py', nproc, '--backend', 'nvlink', '--hidden', hidden, '--experts', experts,
-                       '--topk', topk, '--tokens', tokens, '--max-tokens', maxt, timeout=900)
+                       '--topk', topk, '--tokens', tokens, '--max-tokens', maxt, '--graph', 1, timeout=900)
     assert rc == 0 and 'INTRANODE_PASS' in out, out[-6000:]
 
 

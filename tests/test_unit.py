@@ -187,12 +187,14 @@ def test_heap_layout_regions_fit_and_guards_separate_them(R, M, Mll, H, K, E):
     L = load().heap_layout(R, M, Mll, H, K, E)
     rs = L['row_stride']
     assert rs >= 2 * H and rs % 16 == 0
-    need = {'nd_x': M * rs, 'nd_topk': M * K * 4, 'nd_w': M * K * 4, 'nd_lists': R * M * 4, 'nd_counts': R * 4,
-            'nd_nte': E * 4, 'nc_rows': R * M * 2 * H, 'nc_w': R * M * K * 4, 'nc_send': R * M * 2 * H,
-            'nc_send_w': R * M * K * 4, 'nc_send_off': (R + 1) * 8, 'll_rows': R * Mll * rs, 'll_ids': R * Mll * K * 4,
-            'lc_rows': Mll * K * 2 * H}
+    ins = L['inbox_stride']
+    assert ins % 16 == 0 and ins >= 2 * H + 8 * K + 4                 # 16-bit dispatch row + metadata
+    G = L['max_grid']
+    single = {'inbox': R * M * ins, 'nd_nte': E * 4, 'nd_rcnt': G * R * 4, 'info': R * G * 16, 'prog': R * G * 8}
+    need = {'ll_rows': R * Mll * rs, 'll_ids': R * Mll * K * 4, 'lc_rows': Mll * K * 2 * H}
     regions = [(L['sig'], L['signals_bytes']), (L['local'], L['local_state_bytes'])]
     regions += [(off, need[name]) for name in need for off in L[name]]
+    regions += [(L[name], size) for name, size in single.items()]
     regions.sort()
     guards = sorted(L['guards'])
     gb = L['guard_bytes']
