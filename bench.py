@@ -215,6 +215,13 @@ def main():
     ll = None
     if not args.no_ll and args.impl in ('ours', 'nccl'):
         ll = bench_ll(args, buf, rank, dev, control, graph=args.impl == 'ours')
+        if args.trace and args.impl == 'ours':
+            tr = {k: v for k, v in buf.device_trace().items() if k.startswith('ll.')}
+            everyone = [None] * world
+            dist.all_gather_object(everyone, (rank, tr), group=control)
+            if rank == 0:
+                for r, t in everyone:
+                    log(f'device trace rank {r}: ' + ' '.join(f'{k}={v}' for k, v in t.items()))
 
     # ---- the NCCL build of the same semantics, same inputs, same process group
     nccl = None

@@ -251,16 +251,29 @@ class Buffer:
         return (*out[:5], EventOverlap(ev))
 
     def combine(self, x, handle: DispatchHandle, topk_weights=None, bias=None, config=None,
-                previous_event=None, async_finish: bool = False, allocate_on_comm_stream: bool = False):
+                previous_event=None, async_finish: bool = False, allocate_on_comm_stream: bool = False,
+                pair_pos=None, pair_weights=None):
         """Return every received row to its source and sum per token (fp32, one cast).
 
         ``bias`` (a tensor or a pair of tensors ``[T, H]``) is added before the cast.
+        With ``pair_pos`` / ``pair_weights`` (``[N, K]``), ``x`` holds the expert outputs in
+        permuted order (``[P, H]``) and received row n is ``sum_k pair_weights[n, k] *
+        x[pair_pos[n, k]]`` (fp32, one cast; -1 = no pair): the weighted un-permute runs
+        inside the combine kernel instead of as a separate pass.
         Returns ``(combined_x, combined_topk_weights, event)``.
         """
         biases = () if bias is None else (tuple(bias) if isinstance(bias, (tuple, list)) else (bias,))
+        pairs = None
+        if pair_pos is not None:
+            if pair_weights is None:
+                raise ValueError('pair_pos needs pair_weights')
+            pairs = (pair_pos, pair_weights)
         if self.backend == 'nvlink':
-            fn = lambda: self._engine.combine(x, handle, topk_weights, biases, config)
+            fn = lambda: self._engine.combine(x, handle, topk_weights, biases, config, pairs)
         else:
+            if pairs is not None:
+                from .ops.moe_ops import unpermute
+                x = unpermute(x, pair_pos, pair_weights)
             fn = lambda: self._engine.combine(x, handle, topk_weights, biases)
         out, ev = self._run(fn, previous_event, async_finish, allocate_on_comm_stream)
         return out[0], out[1], EventOverlap(ev)

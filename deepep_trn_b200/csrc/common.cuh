@@ -183,7 +183,9 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
 }
 
 // Copy n bytes with one warp, using the widest access both pointers allow.
-// The 16-byte path keeps eight loads per lane in flight (4 KB per warp).
+// The 16-byte path keeps U loads per lane in flight (U * 512 bytes per warp; U = 16 covers a
+// 7168-wide bf16 row in two round trips, for latency-bound copies of few rows).
+template <int U = 8>
 __device__ __forceinline__ void warp_copy(void* __restrict__ dst, const void* __restrict__ src, int64_t n) {
   const int lane = lane_id();
   const uintptr_t a = reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src);
@@ -192,12 +194,12 @@ __device__ __forceinline__ void warp_copy(void* __restrict__ dst, const void* __
     int4* d = reinterpret_cast<int4*>(dst);
     const int4* s = reinterpret_cast<const int4*>(src);
     int64_t i = lane;
-    for (; i + 224 < m; i += 256) {
-      int4 v[8];
+    for (; i + 32 * (U - 1) < m; i += 32 * U) {
+      int4 v[U];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = s[i + 32 * u];
+      for (int u = 0; u < U; ++u) v[u] = s[i + 32 * u];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) d[i + 32 * u] = v[u];
+      for (int u = 0; u < U; ++u) d[i + 32 * u] = v[u];
     }
     for (; i < m; i += 32) d[i] = s[i];
   } else if ((a & 3) == 0 && (n & 3) == 0) {

@@ -38,7 +38,7 @@ constexpr int kLLRecvThreads = 512;
 __device__ __forceinline__ uint32_t ldv_u32(const uint32_t* p) { return *reinterpret_cast<const volatile uint32_t*>(p); }
 
 // Last CTA of the grid publishes the new epoch of `which` and resets the arrival counter.
-__device__ __forceinline__ void finish_epoch(LocalState* ls, int which, uint32_t e) {
+__device__ __forceinline__ void finish_epoch(LocalState* ls, int which, uint32_t e, int trace_point) {
   __shared__ int s_last;
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -50,6 +50,7 @@ __device__ __forceinline__ void finish_epoch(LocalState* ls, int which, uint32_t
   if (s_last && threadIdx.x == 0) {
     ls->arrive[which] = 0;
     ls->epoch[which] = e;
+    ls->trace[trace_point] = global_ns();
   }
 }
 
@@ -79,6 +80,7 @@ __global__ void __launch_bounds__(kLLThreads) ll_dispatch_send_kernel(LLSendArgs
   __shared__ int32_t s_ids[32];
   __shared__ uint32_t s_mask;
 
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLLSendStart] = global_ns();
   if (blockIdx.x == 0 && tid < R)
     st_release_sys64(&hv.sig(tid)->ll_hdr[slot][me], (static_cast<uint64_t>(e) << 32) | static_cast<uint32_t>(T));
   if (a.T > Mll && blockIdx.x == 0 && tid == 0) report_error(hv.status, kCapacity, 4, me, -1, Mll, a.T);
@@ -160,7 +162,7 @@ __global__ void __launch_bounds__(kLLThreads) ll_dispatch_send_kernel(LLSendArgs
     fence_sys();
     red_add_release_sys(&hv.sig(tid)->ll_cnt[slot][me], static_cast<uint32_t>(t1 - t0));
   }
-  finish_epoch(ls, kEpLLD, e);
+  finish_epoch(ls, kEpLLD, e, kTrLLSendEnd);
 }
 
 void ll_dispatch_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& topk_idx, int64_t num_experts,
@@ -238,6 +240,7 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
   __shared__ int s_src[kLLRecvThreads];
   __shared__ int s_dst[kLLRecvThreads];
   if (tid == 0) s_fail = 0;
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLLRecvStart] = global_ns();
   __syncthreads();
   // headers: one thread per source
   if (tid < R) {
@@ -266,6 +269,7 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
                 static_cast<unsigned long long>(global_ns() - t0));
   }
   __syncthreads();
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLLRecvReady] = global_ns();
   if (tid == 0) {
     int run = 0;
     for (int s = 0; s < R; ++s) {
@@ -328,7 +332,7 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
       const int t2 = s_tok[q], s2 = s_src[q], p = s_dst[q];
       const uint8_t* row = hv.at<uint8_t>(me, hv.L.ll_rows[slot]) + (static_cast<int64_t>(s2) * Mll + t2) * rs;
       const int64_t o = le * RM + p;
-      warp_copy(a.recv_x + o * PB, row, PB);
+      warp_copy<16>(a.recv_x + o * PB, row, PB);
       if (a.use_fp8) {
         const float* sc = reinterpret_cast<const float*>(row + H);
         if (a.ue8m0) {
@@ -362,7 +366,10 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
   __syncthreads();
   if (s_last) {
     if (tid < R) ls->ll_expect[slot][tid] += static_cast<uint32_t>(s_T[tid]);
-    if (tid == 0) ls->arrive[kArLLRecv] = 0;
+    if (tid == 0) {
+      ls->arrive[kArLLRecv] = 0;
+      ls->trace[kTrLLRecvEnd] = global_ns();
+    }
   }
 }
 
@@ -421,14 +428,38 @@ __global__ void __launch_bounds__(kLLThreads) ll_combine_send_kernel(LCSendArgs 
   const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
   constexpr int nwarps = kLLThreads / 32;
   if (tid < R) s_n[tid] = 0;
-  if (tid == 0) {
-    int run = 0;
-    for (int le = 0; le < a.EL; ++le) {
-      s_cnt[le] = run;
-      run += min(a.recv_count[le], static_cast<int>(RM));
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLCSendStart] = global_ns();
+  // exclusive prefix of the per-expert row counts: loads in parallel, warp scans, one pass over
+  // the warp totals (a serial loop of dependent loads costs a memory latency per expert)
+  __shared__ int s_wsum[nwarps];
+  __shared__ int s_carry;
+  if (tid == 0) s_carry = 0;
+  __syncthreads();
+  for (int base = 0; base < a.EL; base += kLLThreads) {
+    const int le = base + tid;
+    const int c = le < a.EL ? min(a.recv_count[le], static_cast<int>(RM)) : 0;
+    int v = c;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, v, d);
+      if (lane >= d) v += u;
     }
-    s_cnt[a.EL] = run;
+    if (lane == 31) s_wsum[warp] = v;
+    __syncthreads();
+    if (tid == 0) {
+      int run = s_carry;
+      for (int w = 0; w < nwarps; ++w) {
+        const int x = s_wsum[w];
+        s_wsum[w] = run;
+        run += x;
+      }
+      s_carry = run;
+    }
+    __syncthreads();
+    if (le < a.EL) s_cnt[le] = s_wsum[warp] + v - c;
+    __syncthreads();
   }
+  if (tid == 0) s_cnt[a.EL] = s_carry;
   __syncthreads();
   const int total = s_cnt[a.EL];
   // valid rows only, one warp per row
@@ -444,7 +475,7 @@ __global__ void __launch_bounds__(kLLThreads) ll_combine_send_kernel(LCSendArgs 
     const int s = sk / K, k = sk % K;
     if (t < 0 || t >= Mll || s < 0 || s >= R) continue;
     uint8_t* dst = hv.base[s] + hv.L.lc_rows[slot] + (static_cast<int64_t>(t) * K + k) * RB;
-    warp_copy(dst, a.x + le * a.x_exp_stride + p * a.x_row_stride, RB);
+    warp_copy<16>(dst, a.x + le * a.x_exp_stride + p * a.x_row_stride, RB);
     if (lane == 0) atomicAdd(&s_n[s], 1u);
   }
   __syncthreads();
@@ -452,7 +483,7 @@ __global__ void __launch_bounds__(kLLThreads) ll_combine_send_kernel(LCSendArgs 
     fence_sys();
     red_add_release_sys(&hv.sig(tid)->lc_cnt[slot][hv.rank], s_n[tid]);
   }
-  finish_epoch(ls, kEpLLC, e);
+  finish_epoch(ls, kEpLLC, e, kTrLCSendEnd);
 }
 
 void ll_combine_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& recv_count, const at::Tensor& src_info,
@@ -508,6 +539,7 @@ __global__ void __launch_bounds__(kLLThreads) ll_combine_recv_kernel(LCRecvArgs 
   // rows expected from every rank = this rank's valid (token, k) entries owned by it
   if (tid < R) s_exp[tid] = 0;
   if (tid == 0) s_fail = 0;
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLCRecvStart] = global_ns();
   __syncthreads();
   for (int64_t i = tid; i < static_cast<int64_t>(a.T) * K; i += kLLThreads) {
     const int64_t g = a.topk_i32 ? static_cast<const int32_t*>(a.topk)[i] : static_cast<const int64_t*>(a.topk)[i];
@@ -520,6 +552,7 @@ __global__ void __launch_bounds__(kLLThreads) ll_combine_recv_kernel(LCRecvArgs 
       s_fail = 1;
   }
   __syncthreads();  // rows acquired by threads < R are read by every thread after this
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLCRecvReady] = global_ns();
   for (int t = blockIdx.x; t < a.T && !s_fail; t += gridDim.x) {
     if (tid < 32) {
       bool valid = false;
@@ -581,7 +614,10 @@ __global__ void __launch_bounds__(kLLThreads) ll_combine_recv_kernel(LCRecvArgs 
   __syncthreads();
   if (s_last) {
     if (tid < R) ls->lc_expect[slot][tid] += s_exp[tid];
-    if (tid == 0) ls->arrive[kArLCRecv] = 0;
+    if (tid == 0) {
+      ls->arrive[kArLCRecv] = 0;
+      ls->trace[kTrLCRecvEnd] = global_ns();
+    }
   }
 }
 

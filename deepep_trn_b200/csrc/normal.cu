@@ -420,6 +420,10 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
     __syncthreads();
   }
   if (tid < R) a.send_start[b * R + tid] = s_start[tid];
+  if (tid == 0) {  // this rank's own range b in its own block (used by combine's pair mode)
+    a.recv_info[(static_cast<int64_t>(me) * kMaxGrid + b) * 2] = s_start[me];
+    a.recv_info[(static_cast<int64_t>(me) * kMaxGrid + b) * 2 + 1] = s_cnt[me];
+  }
   __syncthreads();  // s_fail from the inbox waits
   const bool fail0 = s_fail != 0;
   if (!fail0) {
@@ -749,7 +753,57 @@ struct NcArgs {
   const uint8_t* bias0;
   const uint8_t* bias1;
   int T, H, K;
+  // pair mode: row i of x is sum_k pair_w[i, k] * pairs[pair_pos[i, k]] (fp32, one cast), formed
+  // by the pushing warps from the expert outputs in permuted order (an unpermute fused in)
+  const uint8_t* pairs;     // [P, H] 16-bit, or null
+  const int32_t* pair_pos;  // [N, PK], -1 = no pair
+  const float* pair_w;      // [N, PK]
+  int PK;
 };
+
+// Pair mode: one warp forms row i = sum_k w[i, k] * pairs[pos[i, k]] in fp32 (k ascending) and
+// stores its 16-bit cast at dst.
+template <typename T16>
+__device__ void push_pair_row(const NcArgs& a, int64_t i, uint8_t* dst) {
+  const int lane = lane_id(), PK = a.PK, nch = a.H / 8;
+  const int32_t mp = lane < PK ? a.pair_pos[i * PK + lane] : -1;
+  const float mw = lane < PK ? a.pair_w[i * PK + lane] : 0.f;
+  constexpr int U = 4;
+  for (int c0 = lane; c0 < nch; c0 += 32 * U) {
+    float acc[U][8];
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[u][e] = 0.f;
+    for (int k = 0; k < PK; ++k) {
+      const int32_t p = __shfl_sync(0xffffffffu, mp, k);
+      const float wk = __shfl_sync(0xffffffffu, mw, k);
+      if (p < 0) continue;
+      const int4* src = reinterpret_cast<const int4*>(a.pairs + static_cast<int64_t>(p) * a.H * 2);
+      int4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (c0 + 32 * u < nch) v[u] = src[c0 + 32 * u];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (c0 + 32 * u >= nch) continue;
+        const T16* h = reinterpret_cast<const T16*>(&v[u]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[u][e] += static_cast<float>(h[e]) * wk;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + 32 * u;
+      if (c >= nch) continue;
+      int4 o;
+      T16* oh = reinterpret_cast<T16*>(&o);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) oh[e] = static_cast<T16>(acc[u][e]);
+      reinterpret_cast<int4*>(dst)[c] = o;
+    }
+  }
+}
 
 template <typename T16>
 __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
@@ -769,7 +823,8 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
   if (tid <= R) s_off[tid] = a.recv_off[tid];
   if (tid < R) {
     s_start[tid] = a.recv_info[(static_cast<int64_t>(tid) * kMaxGrid + b) * 2];
-    s_cnt[tid] = tid == me ? 0 : a.recv_info[(static_cast<int64_t>(tid) * kMaxGrid + b) * 2 + 1];
+    // own rows are read from x in place; in pair mode they are formed and written locally too
+    s_cnt[tid] = (tid == me && !a.pairs) ? 0 : a.recv_info[(static_cast<int64_t>(tid) * kMaxGrid + b) * 2 + 1];
   }
   if (b == 0 && tid == 0) ls->trace[kTrNcStart] = global_ns();
   __syncthreads();
@@ -788,21 +843,24 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
       for (int it = pw; it < R * kRoundRows; it += kPushWarps) {
         const int s = (me + 1 + it / kRoundRows) % R;
         const int u = k0 + it % kRoundRows;
-        if (s == me || u >= s_cnt[s]) continue;
+        if (u >= s_cnt[s]) continue;  // (own rows have no count unless in pair mode)
         const int64_t j = s_start[s] + u;
         const int64_t i = s_off[s] + j;
         uint8_t* dst = hv.base[s] + hv.L.inbox + (static_cast<int64_t>(me) * M + j) * IS;
-        warp_copy(dst, a.x + i * a.x_stride, RB);
+        if (a.pairs)
+          push_pair_row<T16>(a, i, dst);
+        else
+          warp_copy(dst, a.x + i * a.x_stride, RB);
         if (a.has_w && lane < K) reinterpret_cast<float*>(dst + RB)[lane] = a.w[i * a.w_stride + lane];
       }
       group_sync(kBarPush, kPushWarps * 32);
-      if (pw == 0 && lane < R && lane != me && s_cnt[lane] > 0) {
+      if (pw == 0 && lane < R && s_cnt[lane] > 0) {
         done = min(s_cnt[lane], k0 + kRoundRows);
         st_release_sys64(hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
                          (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(done));
       }
     }
-    if (pw == 0 && lane < R && lane != me && s_cnt[lane] == 0 && !fail0)
+    if (pw == 0 && lane < R && (lane != me || a.pairs) && s_cnt[lane] == 0 && !fail0)
       st_release_sys64(hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
                        static_cast<uint64_t>(q) << 32);
     (void)done;
@@ -826,7 +884,7 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
       const float* wp = nullptr;
       bool bad = false;
       if (pos >= 0) {
-        if (lane == me) {
+        if (lane == me && !a.pairs) {
           const int64_t i = s_off[me] + pos;
           rp = a.x + i * a.x_stride;
           wp = a.has_w ? a.w + i * a.w_stride : nullptr;
@@ -927,7 +985,8 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
 
 void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const at::Tensor& recv_off,
                 const at::Tensor& recv_info, const at::Tensor& token_pos, const at::Tensor& send_start, at::Tensor out,
-                const OptTensor& out_w, const OptTensor& bias0, const OptTensor& bias1, int64_t grid) {
+                const OptTensor& out_w, const OptTensor& bias0, const OptTensor& bias1, int64_t grid,
+                const OptTensor& pair_pos, const OptTensor& pair_w) {
   const c10::cuda::CUDAGuard guard(out.device());
   HeapView hv = heap.view();
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.element_size() == 2, "combine x must be 16-bit [N, H]");
@@ -965,6 +1024,18 @@ void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const a
   if (bias1.has_value()) {
     TORCH_CHECK(bias1->is_contiguous() && bias1->scalar_type() == x.scalar_type(), "bias dtype/layout");
     a.bias1 = static_cast<const uint8_t*>(bias1->data_ptr());
+  }
+  if (pair_pos.has_value()) {
+    // x holds the expert outputs in permuted order; rows are formed from it by pair_pos / pair_w
+    TORCH_CHECK(pair_w.has_value() && pair_pos->is_contiguous() && pair_pos->scalar_type() == at::kInt &&
+                    pair_w->is_contiguous() && pair_w->scalar_type() == at::kFloat &&
+                    pair_w->sizes() == pair_pos->sizes() && pair_pos->size(1) <= 32,
+                "pair mode needs contiguous pair_pos [N, K] int32 and pair_w [N, K] fp32 (K <= 32)");
+    TORCH_CHECK(x.is_contiguous(), "pair mode needs contiguous expert outputs");
+    a.pairs = a.x;
+    a.pair_pos = pair_pos->data_ptr<int32_t>();
+    a.pair_w = pair_w->data_ptr<float>();
+    a.PK = static_cast<int>(pair_pos->size(1));
   }
   const int G = static_cast<int>(grid);
   TORCH_CHECK(G >= 1 && G <= kMaxGrid && send_start.numel() >= static_cast<int64_t>(G) * hv.R,

@@ -76,7 +76,8 @@ void nd_dispatch(SymmHeap& heap, const at::Tensor& x, const OptTensor& x_scales,
                  bool pad_rows);
 void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const at::Tensor& recv_off,
                 const at::Tensor& recv_info, const at::Tensor& token_pos, const at::Tensor& send_start, at::Tensor out,
-                const OptTensor& out_w, const OptTensor& bias0, const OptTensor& bias1, int64_t grid);
+                const OptTensor& out_w, const OptTensor& bias0, const OptTensor& bias1, int64_t grid,
+                const OptTensor& pair_pos, const OptTensor& pair_w);
 
 // ll.cu
 void ll_dispatch_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& topk_idx, int64_t num_experts,

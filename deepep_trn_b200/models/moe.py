@@ -6,8 +6,7 @@ Forward (per rank, EP group of the Buffer):
     rows = permute(recv) into 128-row padded expert segments          # N10
     h, pre = grouped_gemm(rows, W1, swiglu epilogue)                  # N7 + N8 (tcgen05)
     o = grouped_gemm(h, W2)                                           # N7
-    y_recv = unpermute(o, weights)                                    # N10
-    y = combine(y_recv)                                               # N3
+    y = combine(o, pairs=(pos, weights))  (weighted un-permute fused)  # N10 + N3
 Backward reuses the dispatch handle: the gradient of combine is a cached dispatch
 and the gradient of dispatch is a combine (whose weight channel carries the
 routing-weight gradients home). Expert weight gradients come from the variable-K
@@ -72,10 +71,9 @@ class _MoEFunction(torch.autograd.Function):
             rows, pos, offsets, counts = MO.permute(recv_x, recv_idx, EL, per_expert)
         with timer.stage('moe.experts'):
             h, pre, o = _expert_forward(rows, offsets, W1, W2)
-        with timer.stage('moe.unpermute'):
-            y_recv = MO.unpermute(o, pos, recv_w)
         with timer.stage('moe.combine'):
-            y, _, _ = buf.combine(y_recv, handle)
+            # the weighted un-permute (sum_k w * o[pos]) is formed inside the combine kernel
+            y, _, _ = buf.combine(o, handle, pair_pos=pos, pair_weights=recv_w)
         ctx.save_for_backward(x, Wr, W1, W2, idx, w, recv_w, pos, offsets, counts, rows, pre, h, o)
         ctx.buf, ctx.handle, ctx.num_experts = buf, handle, num_experts
         return y
@@ -187,10 +185,9 @@ class MoELayer(nn.Module):
             h, _ = G.grouped_gemm_fp8(rq, rs, q1, t1, offsets, epilogue='swiglu', save_preact=False)
             hq, hs = quantize_fp8(h, round_scale=True)
             o = G.grouped_gemm_fp8(hq, hs, q2, t2, offsets)
-        with timer.stage('moe.unpermute'):
-            y_recv = MO.unpermute(o, pos, recv_w)
         with timer.stage('moe.combine'):
-            y, _, _ = buf.combine(y_recv, handle)
+            # the weighted un-permute (sum_k w * o[pos]) is formed inside the combine kernel
+            y, _, _ = buf.combine(o, handle, pair_pos=pos, pair_weights=recv_w)
         return y
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:

@@ -108,7 +108,11 @@ class NvlinkEngine:
                 'dispatch.cta0_pushed': d(0, 4), 'dispatch.cta0_received': d(0, 5), 'dispatch.total': d(0, 6),
                 'gap.dispatch_to_combine': d(6, 16), 'combine.cta0_pushed': d(16, 17),
                 'combine.cta0_reduced': d(16, 18), 'combine.total': d(16, 19),
-                'step.dispatch_to_combine_end': d(0, 19)}
+                'step.dispatch_to_combine_end': d(0, 19),
+                'll.dispatch_send': d(24, 25), 'll.gap_send_to_recv': d(25, 26), 'll.dispatch_recv_wait': d(26, 27),
+                'll.dispatch_recv_copy': d(27, 28), 'll.gap_to_combine': d(28, 32), 'll.combine_send': d(32, 33),
+                'll.gap_send_to_recv2': d(33, 34), 'll.combine_recv_wait': d(34, 35),
+                'll.combine_recv_reduce': d(35, 36), 'll.total': d(24, 36)}
 
     def barrier(self) -> None:
         """Device-side barrier over the EP group (epoch flags in peer memory, bounded wait)."""
@@ -264,9 +268,11 @@ class NvlinkEngine:
             recv_w = recv_w.to(topk_weights.dtype)
         return out_x, recv_topk, recv_w, per_expert, new, EventOverlap()
 
-    def combine(self, x, handle, topk_weights, bias, config):
+    def combine(self, x, handle, topk_weights, bias, config, pairs=None):
+        """``pairs = (pair_pos [N, K] int32, pair_w [N, K])``: ``x`` holds expert outputs in
+        permuted order and row n is formed in the kernel as sum_k pair_w[n, k] * x[pair_pos[n, k]]."""
         self.check()
-        N, H = x.shape
+        N, H = (pairs[0].shape[0], x.shape[1]) if pairs is not None else x.shape
         if handle.num_recv is not None and N != handle.num_recv:
             raise ValueError(f'combine got {N} rows, dispatch delivered {handle.num_recv}')
         if x.dtype not in (torch.bfloat16, torch.float16):
@@ -279,11 +285,16 @@ class NvlinkEngine:
             if topk_weights is not None else None
         b = [t.contiguous() for t in bias]
         xc = x if (x.stride(1) == 1 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0) else x.contiguous()
+        pp = pw = None
+        if pairs is not None:
+            xc = x.contiguous()
+            pp = pairs[0] if pairs[0].dtype == torch.int32 else pairs[0].to(torch.int32)
+            pp, pw = _contig(pp), _contig(_f32(pairs[1]))
         with timer.stage('combine'):
             self.C.nc_combine(self.heap, xc,
                               _contig(_f32(topk_weights)) if topk_weights is not None else None,
                               handle.recv_off, handle.recv_info, handle.token_pos, handle.send_start, out, out_w,
-                              b[0] if len(b) > 0 else None, b[1] if len(b) > 1 else None, handle.grid)
+                              b[0] if len(b) > 0 else None, b[1] if len(b) > 1 else None, handle.grid, pp, pw)
         if out_w is not None and topk_weights.dtype != torch.float32:
             out_w = out_w.to(topk_weights.dtype)
         return out, out_w, EventOverlap()

@@ -6,7 +6,8 @@ torchrun --nnodes 1 --nproc-per-node 4 --master-addr 127.0.0.1 tests/dist/intran
 Scenarios (the same list as deep_ep_trn's tests/dist/test_intranode.py, plus the API paths
 the reference leaves unimplemented): layout, dispatch rows / ids / weights / sources /
 per-expert counts, cached dispatch, identity and emulated-expert combine, combine weights,
-bias, fp8 (in-kernel quantisation and pre-quantised tuples), expert_alignment,
+bias, pair mode (the weighted un-permute inside combine), fp8 (in-kernel quantisation and
+pre-quantised tuples), expert_alignment,
 num_worst_tokens (also under CUDA-graph capture), async_finish / previous_event /
 allocate_on_comm_stream, and the same op on several grid sizes (NVLink backend).
 """
@@ -86,6 +87,13 @@ def main():
         got = sc.host(out).float()
         rel = float((got - ref).abs().mean() / ref.abs().mean().clamp_min(1e-9)) if T else 0.0
         assert torch.allclose(got, ref, rtol=2e-2, atol=2e-3) and rel < 1e-2, (kind, 'expert combine', rel)
+        # pair mode: expert outputs in permuted order, the weighted un-permute formed by the combine
+        from deepep_trn_b200.ops import moe_ops as MO
+        y = (rx.float() * (1.0 + 0.25 * torch.arange(H) / H)).to(torch.bfloat16)
+        rows, ppos, _, _ = MO.permute(sc.dev(y), sc.dev(ridx), EL)
+        fused, _, _ = buf.combine(rows, handle, pair_pos=ppos, pair_weights=sc.dev(rw))
+        split, _, _ = buf.combine(MO.unpermute(rows, ppos, sc.dev(rw)), handle)
+        assert torch.equal(sc.host(fused), sc.host(split)), (kind, 'pair-mode combine')
         bias = torch.randn(T, H, generator=torch.Generator().manual_seed(7 + sc.rank)).to(torch.bfloat16)
         out, _, _ = buf.combine(sc.dev(rx), handle, bias=sc.dev(bias))
         assert torch.equal(sc.host(out), (x.float() * visits + bias.float()).to(torch.bfloat16)), (kind, 'bias')
