@@ -204,3 +204,14 @@ def test_heap_layout_regions_fit_and_guards_separate_them(R, M, Mll, H, K, E):
     for (g, (nxt, _)) in zip(guards, regions[1:]):
         assert g + gb <= nxt                                          # the guard ends before the next region
     assert guards[-1] + gb <= L['total']
+
+
+def test_heap_fits_the_headline_config_in_a_fixed_budget():
+    """EP8, 4096 tokens per rank, H=7168, top-8 of 256 experts, 128 low-latency tokens: the
+    symmetric heap (one inbox shared by dispatch and combine, no double buffering) stays
+    under 0.6 GB per GPU."""
+    from deepep_trn_b200.ops._ext import available
+    if not available():
+        pytest.skip('extension not built')
+    from deepep_trn_b200.parallel.symm import HeapSpec, heap_bytes
+    assert heap_bytes(8, HeapSpec(4096, 128, 7168, 8, 256)) < 0.6e9
