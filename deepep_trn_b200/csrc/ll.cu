@@ -211,10 +211,14 @@ struct LLRecvArgs {
   int64_t* wait_stats;      // [R] or null
   int H, K, E;
   int use_fp8, ue8m0;
+  int split;                // CTAs per local expert
 };
 
-// grid: one CTA per local expert. One pass over the (src, token) slots of all
-// sources flattened in (src, token) order, 512 slots per tile.
+// grid: `split` CTAs per local expert. Every CTA of an expert walks the (src, token) slots of
+// all sources flattened in (src, token) order, 512 slots per tile, up to the end of its
+// share of the slots: the ids of the earlier slots give it the position of its first row
+// (no communication between the CTAs), and it copies the rows of its own slots. The last
+// CTA of the expert, which has walked every slot, writes the counts and layout_range.
 __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecvArgs a) {
   const HeapView& hv = a.hv;
   LocalState* ls = hv.local();
@@ -223,7 +227,8 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
   const int me = hv.rank, R = hv.R, Mll = hv.cfg.Mll;
   const int64_t rs = hv.L.row_stride;
   const int H = a.H, K = a.K, EL = a.E / R;
-  const int le = blockIdx.x;
+  const int le = blockIdx.x / a.split, part = blockIdx.x % a.split;
+  const bool last_part = part == a.split - 1;
   const int32_t want = me * EL + le;
   const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
   constexpr int nwarps = kLLRecvThreads / 32;
@@ -264,7 +269,7 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
       if (!wait_epoch(&hv.sig(me)->ll_cnt[slot][tid], target, hv.timeout_ns, hv.status, kTimeoutLLRow, 5, me, tid))
         s_fail = 1;
     }
-    if (a.wait_stats && le == 0)
+    if (a.wait_stats && blockIdx.x == 0)
       atomicAdd(reinterpret_cast<unsigned long long*>(&a.wait_stats[tid]),
                 static_cast<unsigned long long>(global_ns() - t0));
   }
@@ -280,11 +285,14 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
   }
   __syncthreads();
   const int total = s_toff[R];
+  const int lo_slot = static_cast<int>(static_cast<int64_t>(total) * part / a.split);
+  const int hi_slot = static_cast<int>(static_cast<int64_t>(total) * (part + 1) / a.split);
+  __shared__ int s_own[kLLRecvThreads];
   int running = 0;
-  for (int tile = 0; tile < total; tile += kLLRecvThreads) {
+  for (int tile = 0; tile < hi_slot; tile += kLLRecvThreads) {
     const int i = tile + tid;
     int hit = -1, s = 0, t = 0;
-    if (i < total && !s_fail) {
+    if (i < hi_slot && !s_fail) {
       while (s + 1 < R && s_toff[s + 1] <= i) ++s;
       t = i - s_toff[s];
       const int64_t slot_row = static_cast<int64_t>(s) * Mll + t;
@@ -320,15 +328,20 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
     if (hit >= 0) {
       const int q = s_wcnt[warp] + __popc(b & lanemask_lt());
       const int p = running + q;
+      const bool own = i >= lo_slot;
       s_tok[q] = t;
       s_src[q] = s;
       s_dst[q] = p;
-      a.src_info[le * RM + p] = t;
-      a.pair_meta[le * RM + p] = s * K + hit;
+      s_own[q] = own;
+      if (own) {
+        a.src_info[le * RM + p] = t;
+        a.pair_meta[le * RM + p] = s * K + hit;
+      }
       atomicAdd(&s_bcnt[s], 1);
     }
     __syncthreads();  // rows acquired by other threads are ordered by the barrier
     for (int q = warp; q < tile_total; q += nwarps) {
+      if (!s_own[q]) continue;
       const int t2 = s_tok[q], s2 = s_src[q], p = s_dst[q];
       const uint8_t* row = hv.at<uint8_t>(me, hv.L.ll_rows[slot]) + (static_cast<int64_t>(s2) * Mll + t2) * rs;
       const int64_t o = le * RM + p;
@@ -346,15 +359,17 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
     running += tile_total;
     __syncthreads();
   }
-  if (tid < R) {
-    int start = 0;
-    for (int s = 0; s < tid; ++s) start += s_bcnt[s];
-    a.layout_range[le * R + tid] = (static_cast<int64_t>(start) << 32) | static_cast<int64_t>(s_bcnt[tid]);
-  }
-  for (int64_t p = running + tid; p < RM; p += kLLRecvThreads) a.src_info[le * RM + p] = -1;
-  if (tid == 0) {
-    a.recv_count[le] = running;
-    if (a.cum_stats) atomicAdd(&a.cum_stats[le], running);
+  if (last_part) {
+    if (tid < R) {
+      int start = 0;
+      for (int s = 0; s < tid; ++s) start += s_bcnt[s];
+      a.layout_range[le * R + tid] = (static_cast<int64_t>(start) << 32) | static_cast<int64_t>(s_bcnt[tid]);
+    }
+    for (int64_t p = running + tid; p < RM; p += kLLRecvThreads) a.src_info[le * RM + p] = -1;
+    if (tid == 0) {
+      a.recv_count[le] = running;
+      if (a.cum_stats) atomicAdd(&a.cum_stats[le], running);
+    }
   }
   // the last expert CTA records the slots consumed from each source
   __shared__ int s_last;
@@ -398,7 +413,9 @@ void ll_dispatch_recv(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_s
   a.pair_meta = pair_meta.data_ptr<int32_t>();
   if (cum_stats.has_value()) a.cum_stats = cum_stats->data_ptr<int32_t>();
   if (wait_stats.has_value()) a.wait_stats = wait_stats->data_ptr<int64_t>();
-  ll_dispatch_recv_kernel<<<EL, kLLRecvThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  // spread the copies over about 128 CTAs when there are few local experts
+  a.split = EL >= 128 ? 1 : std::max(1, std::min(8, 128 / EL));
+  ll_dispatch_recv_kernel<<<EL * a.split, kLLRecvThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
