@@ -11,11 +11,11 @@
 //      every CTA knows where its range starts in each destination's block, writes the
 //      token -> row map (token_pos) and tells each destination (first row, rows) of
 //      its range; CTA 0 publishes this rank's row totals to every destination.
-//   2. warps 0..7 push: each token row goes straight from x to every other rank that
+//   2. warps 0..6 push: each token row goes straight from x to every other rank that
 //      owns one of its experts, 16-byte stores into that rank's inbox over NVLink
 //      (fp8 e4m3 + 1x128 scales quantised in registers on the way when asked), with
 //      the token's top-k ids, weights and index appended; after each round of tokens
-//      the CTA publishes per destination how many rows of its range have landed.
+//      warp 7 publishes per destination how many rows of the CTA's range have landed.
 //   3. warps 8..15 receive: as soon as every source's total is in, CTA 0 publishes the
 //      receive size to the host; every CTA then copies, for each source s, the rows
 //      that s's CTA b pushed (as its progress word advances) from the inbox to recv_x
@@ -46,8 +46,13 @@ constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kPushWarps = 8;                     // warps [0, 8) send, [8, 16) receive / reduce
 constexpr int kRecvWarps = kWarps - kPushWarps;
-constexpr int kRoundTok = 2 * kPushWarps;         // dispatch: tokens per progress publication
-constexpr int kRoundRows = 2 * kPushWarps;        // combine: rows per source per progress publication
+// Of the sending warps, the last only publishes progress: after each round the others arrive
+// on a named barrier without waiting, and it releases the round's progress words, so no
+// pushing warp ever waits for a system-scope release to drain its NVLink stores.
+constexpr int kMovers = kPushWarps - 1;
+constexpr int kPublisher = kPushWarps - 1;
+constexpr int kRoundTok = 2 * kMovers;            // dispatch: tokens per progress publication
+constexpr int kRoundRows = 2 * kMovers;           // combine: rows per source per progress publication
 constexpr int kBarPush = 1, kBarRecv = 2;         // named barriers of the two warp groups
 
 __device__ __forceinline__ int32_t ldv_i32(const int32_t* p) { return *reinterpret_cast<const volatile int32_t*>(p); }
@@ -56,6 +61,11 @@ __device__ __forceinline__ uint32_t ldv_u32(const uint32_t* p) {
 }
 __device__ __forceinline__ void group_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+// Arrive on a named barrier without waiting (the writes before it are performed for the
+// threads that wait on it).
+__device__ __forceinline__ void group_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 __device__ __forceinline__ int warp_sum(int v) {
 #pragma unroll
@@ -450,34 +460,40 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
   if (warp < kPushWarps) {
     // ------------------------------------------------------------ push (warps 0..7)
     const int pw = warp;
-    uint64_t* prog_base = nullptr;
-    int32_t done = 0;   // lane r < R of warp 0: rows of my range pushed to destination r
     if (!fail0) {
-      for (int rt = t0; rt < t1; rt += kRoundTok) {
-        const int re = min(rt + kRoundTok, t1);
-        for (int t = rt + pw; t < re; t += kPushWarps) {
-          uint32_t m = 0;
-          if (lane < R) {
-            const int32_t p = a.token_pos[static_cast<int64_t>(t) * R + lane];
-            s_pos[pw][lane] = p;
-            m = (p >= 0 && lane != me) ? 1u : 0u;
+      if (pw != kPublisher) {
+        for (int rt = t0; rt < t1; rt += kRoundTok) {
+          const int re = min(rt + kRoundTok, t1);
+          for (int t = rt + pw; t < re; t += kMovers) {
+            uint32_t m = 0;
+            if (lane < R) {
+              const int32_t p = a.token_pos[static_cast<int64_t>(t) * R + lane];
+              s_pos[pw][lane] = p;
+              m = (p >= 0 && lane != me) ? 1u : 0u;
+            }
+            const uint32_t dmask = __ballot_sync(0xffffffffu, m);
+            __syncwarp();
+            if (dmask) push_token<T16>(a, t, dmask, s_pos[pw]);
+            __syncwarp();
           }
-          const uint32_t dmask = __ballot_sync(0xffffffffu, m);
-          __syncwarp();
-          if (dmask) push_token<T16>(a, t, dmask, s_pos[pw]);
-          __syncwarp();
+          group_arrive(kBarPush, kPushWarps * 32);
         }
-        group_sync(kBarPush, kPushWarps * 32);
-        if (pw == 0 && lane < R && lane != me) {
-          for (int t = rt; t < re; ++t) done += a.token_pos[static_cast<int64_t>(t) * R + lane] >= 0 ? 1 : 0;
-          prog_base = hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b;
-          st_release_sys64(prog_base, (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(done));
+      } else {
+        // lane r < R: rows of my range pushed to destination r, released after each round
+        int32_t done = 0;
+        uint64_t* prog = lane < R ? hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b
+                                  : nullptr;
+        for (int rt = t0; rt < t1; rt += kRoundTok) {
+          const int re = min(rt + kRoundTok, t1);
+          group_sync(kBarPush, kPushWarps * 32);
+          if (lane < R && lane != me) {
+            for (int t = rt; t < re; ++t) done += a.token_pos[static_cast<int64_t>(t) * R + lane] >= 0 ? 1 : 0;
+            st_release_sys64(prog, (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(done));
+          }
         }
+        // an empty range still tells every destination that it is complete
+        if (t1 <= t0 && lane < R && lane != me) st_release_sys64(prog, static_cast<uint64_t>(q) << 32);
       }
-      // an empty range still tells every destination that it is complete
-      if (t1 <= t0 && pw == 0 && lane < R && lane != me)
-        st_release_sys64(hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
-                         static_cast<uint64_t>(q) << 32);
     }
   } else {
     // ------------------------------------------------------------ receive (warps 8..15)
@@ -837,10 +853,17 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
     const int pw = warp;
     int32_t maxc = 0;
     for (int s = 0; s < R; ++s) maxc = max(maxc, s_cnt[s]);
-    int32_t done = 0;
     for (int k0 = 0; k0 < maxc && !fail0; k0 += kRoundRows) {
+      if (pw == kPublisher) {
+        // release the round's progress once the moving warps have arrived
+        group_sync(kBarPush, kPushWarps * 32);
+        if (lane < R && s_cnt[lane] > 0)
+          st_release_sys64(hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
+                           (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(min(s_cnt[lane], k0 + kRoundRows)));
+        continue;
+      }
       // items of the round: for each source (rotated), rows [k0, k0 + kRoundRows) of its range
-      for (int it = pw; it < R * kRoundRows; it += kPushWarps) {
+      for (int it = pw; it < R * kRoundRows; it += kMovers) {
         const int s = (me + 1 + it / kRoundRows) % R;
         const int u = k0 + it % kRoundRows;
         if (u >= s_cnt[s]) continue;  // (own rows have no count unless in pair mode)
@@ -853,17 +876,11 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
           warp_copy(dst, a.x + i * a.x_stride, RB);
         if (a.has_w && lane < K) reinterpret_cast<float*>(dst + RB)[lane] = a.w[i * a.w_stride + lane];
       }
-      group_sync(kBarPush, kPushWarps * 32);
-      if (pw == 0 && lane < R && s_cnt[lane] > 0) {
-        done = min(s_cnt[lane], k0 + kRoundRows);
-        st_release_sys64(hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
-                         (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(done));
-      }
+      group_arrive(kBarPush, kPushWarps * 32);
     }
-    if (pw == 0 && lane < R && (lane != me || a.pairs) && s_cnt[lane] == 0 && !fail0)
+    if (pw == kPublisher && lane < R && (lane != me || a.pairs) && s_cnt[lane] == 0 && !fail0)
       st_release_sys64(hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
                        static_cast<uint64_t>(q) << 32);
-    (void)done;
   } else {
     // ------------------------------------------------------------ reduce my tokens (warps 8..15)
     const int rw = warp - kPushWarps;
