@@ -20,10 +20,14 @@ namespace b200ep {
 // Device trace points: the last op of each kind stamps %globaltimer at fixed phases.
 enum TracePoint : int {
   // normal dispatch: kernel start, scan done (counts published), peers' counts in, host
-  // notified, CTA 0's pushes done, CTA 0's receives done, kernel end
-  kTrNdStart = 0, kTrNdScanned, kTrNdCounts, kTrNdNotified, kTrNdPushed, kTrNdRecvd, kTrNdEnd,
-  // normal combine: kernel start, CTA 0's pushes done, CTA 0's reduction done, kernel end
-  kTrNcStart = 16, kTrNcPushed, kTrNcReduced, kTrNcEnd,
+  // notified, CTA 0's pushes done, CTA 0's receives done, kernel end, CTA 0's last progress
+  // word released
+  kTrNdStart = 0, kTrNdScanned, kTrNdCounts, kTrNdNotified, kTrNdPushed, kTrNdRecvd, kTrNdEnd, kTrNdPublished,
+  kTrNdWaitNs = 8,  // not a stamp: mean ns a receiving warp of CTA 0 waited for progress words
+  // normal combine: kernel start, CTA 0's pushes done, CTA 0's reduction done, kernel end,
+  // CTA 0's last progress word released
+  kTrNcStart = 16, kTrNcPushed, kTrNcReduced, kTrNcEnd, kTrNcPublished,
+  kTrNcWaitNs = 21,  // not a stamp: mean ns a reducing warp of CTA 0 waited for progress words
   kTrLLSendStart = 24, kTrLLSendEnd, kTrLLRecvStart, kTrLLRecvReady, kTrLLRecvEnd,
   kTrLCSendStart = 32, kTrLCSendEnd, kTrLCRecvStart, kTrLCRecvReady, kTrLCRecvEnd,
   kTracePoints = 40,

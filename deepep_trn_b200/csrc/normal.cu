@@ -46,13 +46,12 @@ constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kPushWarps = 8;                     // warps [0, 8) send, [8, 16) receive / reduce
 constexpr int kRecvWarps = kWarps - kPushWarps;
-// Of the sending warps, the last only publishes progress: after each round the others arrive
-// on a named barrier without waiting, and it releases the round's progress words, so no
-// pushing warp ever waits for a system-scope release to drain its NVLink stores.
+// Of the sending warps, the last only publishes progress: all eight meet on a named barrier
+// after each round, then the publisher releases that round's progress words while the
+// others push the next round, so a system-scope release overlaps a round of pushes.
 constexpr int kMovers = kPushWarps - 1;
 constexpr int kPublisher = kPushWarps - 1;
-constexpr int kRoundTok = 2 * kMovers;            // dispatch: tokens per progress publication
-constexpr int kRoundRows = 2 * kMovers;           // combine: rows per source per progress publication
+constexpr int kDefaultRound = 2 * kMovers;        // tokens (dispatch) / rows per source (combine) per publication
 constexpr int kBarPush = 1, kBarRecv = 2;         // named barriers of the two warp groups
 
 __device__ __forceinline__ int32_t ldv_i32(const int32_t* p) { return *reinterpret_cast<const volatile int32_t*>(p); }
@@ -62,11 +61,7 @@ __device__ __forceinline__ uint32_t ldv_u32(const uint32_t* p) {
 __device__ __forceinline__ void group_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
-// Arrive on a named barrier without waiting (the writes before it are performed for the
-// threads that wait on it).
-__device__ __forceinline__ void group_arrive(int id, int nthreads) {
-  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
-}
+
 __device__ __forceinline__ int warp_sum(int v) {
 #pragma unroll
   for (int m = 16; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
@@ -196,6 +191,18 @@ __device__ __forceinline__ void acc8(float (&acc)[8], const int4& raw) {
   for (int i = 0; i < 8; ++i) acc[i] += static_cast<float>(h[i]);
 }
 
+// Tokens (dispatch) or rows per source (combine) between two progress publications of a
+// CTA: B200EP_PROGRESS_ROUND, default two per moving warp; a large value publishes once,
+// at the end of the CTA's pushes.
+int progress_round() {
+  static const int r = [] {
+    const char* v = getenv("B200EP_PROGRESS_ROUND");
+    const int n = v ? atoi(v) : 0;
+    return n > 0 ? n : kDefaultRound;
+  }();
+  return r;
+}
+
 }  // namespace
 
 // ============================================================================ dispatch
@@ -227,6 +234,7 @@ struct NdArgs {
   int T, H, K, E;
   uint64_t ticket;
   int pad_rows;           // fill the metadata of rows [N, capacity) (sync-free sizing)
+  int round;              // tokens per progress publication
 };
 
 // Push warp `pw` writes token t to every destination of `dmask`: payload, scales, ids,
@@ -365,7 +373,10 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
   if (tid == 0) s_fail = 0;
   if (tid < R) s_cnt[tid] = 0;
   if (a.T > M && b == 0 && tid == 0) report_error(hv.status, kCapacity, 1, me, -1, M, a.T);
-  if (b == 0 && tid == 0) ls->trace[kTrNdStart] = global_ns();
+  if (b == 0 && tid == 0) {
+    ls->trace[kTrNdStart] = global_ns();
+    ls->trace[kTrNdWaitNs] = 0;
+  }
   __syncthreads();
   wait_inboxes_free(hv, q, &s_fail);
 
@@ -462,8 +473,8 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
     const int pw = warp;
     if (!fail0) {
       if (pw != kPublisher) {
-        for (int rt = t0; rt < t1; rt += kRoundTok) {
-          const int re = min(rt + kRoundTok, t1);
+        for (int rt = t0; rt < t1; rt += a.round) {
+          const int re = min(rt + a.round, t1);
           for (int t = rt + pw; t < re; t += kMovers) {
             uint32_t m = 0;
             if (lane < R) {
@@ -476,15 +487,15 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
             if (dmask) push_token<T16>(a, t, dmask, s_pos[pw]);
             __syncwarp();
           }
-          group_arrive(kBarPush, kPushWarps * 32);
+          group_sync(kBarPush, kPushWarps * 32);
         }
       } else {
         // lane r < R: rows of my range pushed to destination r, released after each round
         int32_t done = 0;
         uint64_t* prog = lane < R ? hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b
                                   : nullptr;
-        for (int rt = t0; rt < t1; rt += kRoundTok) {
-          const int re = min(rt + kRoundTok, t1);
+        for (int rt = t0; rt < t1; rt += a.round) {
+          const int re = min(rt + a.round, t1);
           group_sync(kBarPush, kPushWarps * 32);
           if (lane < R && lane != me) {
             for (int t = rt; t < re; ++t) done += a.token_pos[static_cast<int64_t>(t) * R + lane] >= 0 ? 1 : 0;
@@ -493,6 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
         }
         // an empty range still tells every destination that it is complete
         if (t1 <= t0 && lane < R && lane != me) st_release_sys64(prog, static_cast<uint64_t>(q) << 32);
+        if (b == 0 && lane == 0) ls->trace[kTrNdPublished] = global_ns();
       }
     }
   } else {
@@ -592,6 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
           }
         }
       }
+      uint64_t waited = 0;  // ns this warp spent waiting for progress words (CTA 0 reports it)
       // rows pushed by other ranks: for each source (rotated), the rows of its CTA b's range
       for (int k = 1; k < R && !rfail; ++k) {
         const int s = (me + R - k) % R;
@@ -617,7 +630,9 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
           if (u >= seen) {
             // one lane polls; __syncwarp orders the other lanes' reads of the rows after its acquire
             int64_t v = 0;
+            const uint64_t tw = global_ns();
             if (lane == 0) v = wait_progress(prog, q, u + 1, hv, 1, s);
+            waited += global_ns() - tw;
             seen = __shfl_sync(0xffffffffu, v, 0);
             __syncwarp();
             if (seen < 0) {
@@ -638,6 +653,9 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
         group_sync(kBarRecv, kRecvWarps * 32);
       }
       if (rt == 0 && s_rfail) report_error(hv.status, kTimeoutReady, 1, me, -1, 0, 0, 3);
+      if (b == 0 && lane == 0)
+        atomicAdd(reinterpret_cast<unsigned long long*>(&ls->trace[kTrNdWaitNs]),
+                  static_cast<unsigned long long>(waited / kRecvWarps));
     }
     // sync-free sizing: the rows past N carry no expert (-1), weight 0 and source -1
     if (a.pad_rows) {
@@ -746,6 +764,7 @@ void nd_dispatch(SymmHeap& heap, const at::Tensor& x, const OptTensor& x_scales,
   a.recv_src = recv_src.data_ptr();
   a.recv_src_i32 = recv_src.scalar_type() == at::kInt;
   a.pad_rows = pad_rows ? 1 : 0;
+  a.round = progress_round();
   void* fn = a.x_fp16 ? reinterpret_cast<void*>(nd_kernel<__half>) : reinterpret_cast<void*>(nd_kernel<__nv_bfloat16>);
   void* args[] = {&a};
   // cooperative: CTAs wait for one another (grid barrier) and for peers' CTAs, so all must be resident
@@ -775,6 +794,7 @@ struct NcArgs {
   const int32_t* pair_pos;  // [N, PK], -1 = no pair
   const float* pair_w;      // [N, PK]
   int PK;
+  int round;                // rows per source per progress publication
 };
 
 // Pair mode: one warp forms row i = sum_k w[i, k] * pairs[pos[i, k]] in fp32 (k ascending) and
@@ -842,7 +862,10 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
     // own rows are read from x in place; in pair mode they are formed and written locally too
     s_cnt[tid] = (tid == me && !a.pairs) ? 0 : a.recv_info[(static_cast<int64_t>(tid) * kMaxGrid + b) * 2 + 1];
   }
-  if (b == 0 && tid == 0) ls->trace[kTrNcStart] = global_ns();
+  if (b == 0 && tid == 0) {
+    ls->trace[kTrNcStart] = global_ns();
+    ls->trace[kTrNcWaitNs] = 0;
+  }
   __syncthreads();
   wait_inboxes_free(hv, q, &s_fail);
   __syncthreads();
@@ -853,19 +876,20 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
     const int pw = warp;
     int32_t maxc = 0;
     for (int s = 0; s < R; ++s) maxc = max(maxc, s_cnt[s]);
-    for (int k0 = 0; k0 < maxc && !fail0; k0 += kRoundRows) {
+    const int RR = a.round;
+    for (int k0 = 0; k0 < maxc && !fail0; k0 += RR) {
       if (pw == kPublisher) {
-        // release the round's progress once the moving warps have arrived
+        // release the round's progress once the moving warps have met here
         group_sync(kBarPush, kPushWarps * 32);
         if (lane < R && s_cnt[lane] > 0)
           st_release_sys64(hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
-                           (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(min(s_cnt[lane], k0 + kRoundRows)));
+                           (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(min(s_cnt[lane], k0 + RR)));
         continue;
       }
-      // items of the round: for each source (rotated), rows [k0, k0 + kRoundRows) of its range
-      for (int it = pw; it < R * kRoundRows; it += kMovers) {
-        const int s = (me + 1 + it / kRoundRows) % R;
-        const int u = k0 + it % kRoundRows;
+      // items of the round: for each source (rotated), rows [k0, k0 + RR) of its range
+      for (int it = pw; it < R * RR; it += kMovers) {
+        const int s = (me + 1 + it / RR) % R;
+        const int u = k0 + it % RR;
         if (u >= s_cnt[s]) continue;  // (own rows have no count unless in pair mode)
         const int64_t j = s_start[s] + u;
         const int64_t i = s_off[s] + j;
@@ -876,11 +900,12 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
           warp_copy(dst, a.x + i * a.x_stride, RB);
         if (a.has_w && lane < K) reinterpret_cast<float*>(dst + RB)[lane] = a.w[i * a.w_stride + lane];
       }
-      group_arrive(kBarPush, kPushWarps * 32);
+      group_sync(kBarPush, kPushWarps * 32);
     }
     if (pw == kPublisher && lane < R && (lane != me || a.pairs) && s_cnt[lane] == 0 && !fail0)
       st_release_sys64(hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
                        static_cast<uint64_t>(q) << 32);
+    if (pw == kPublisher && b == 0 && lane == 0) ls->trace[kTrNcPublished] = global_ns();
   } else {
     // ------------------------------------------------------------ reduce my tokens (warps 8..15)
     const int rw = warp - kPushWarps;
@@ -894,6 +919,7 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
     const uint8_t* inbox = hv.at<uint8_t>(me, hv.L.inbox);
     const int nch = H / 8;
     bool wfail = fail0;
+    uint64_t waited = 0;   // ns this lane spent waiting for progress words (CTA 0 reports it)
     for (int t = t0 + rw; t < t1 && !wfail; t += kRecvWarps) {
       // this token's rows: one per rank that received it
       int32_t pos = lane < R ? a.token_pos[static_cast<int64_t>(t) * R + lane] : -1;
@@ -908,8 +934,10 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
         } else {
           const int64_t want = pos - a.send_start[b * R + lane] + 1;
           if (want > s_seen[rw][lane]) {
+            const uint64_t tw = global_ns();
             const int64_t v = wait_progress(hv.at<uint64_t>(me, hv.L.prog) + static_cast<int64_t>(lane) * kMaxGrid + b,
                                             q, want, hv, 3, lane);
+            waited += global_ns() - tw;
             if (v < 0) bad = true; else s_seen[rw][lane] = v;
           }
           rp = inbox + (static_cast<int64_t>(lane) * M + pos) * IS;
@@ -993,6 +1021,12 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
       __syncwarp();
     }
     if (wfail && lane == 0) report_error(hv.status, kTimeoutCombine, 3, me, -1, 0, 0, 2);
+    if (b == 0) {
+      // mean wait per reducing warp (the slowest lane of each warp), for the device trace
+      for (int m = 16; m >= 1; m >>= 1) waited = max(waited, __shfl_xor_sync(0xffffffffu, waited, m));
+      if (lane == 0) atomicAdd(reinterpret_cast<unsigned long long*>(&ls->trace[kTrNcWaitNs]),
+                               static_cast<unsigned long long>(waited / kRecvWarps));
+    }
   }
   if (b == 0 && (tid == 0 || tid == kPushWarps * 32))
     ls->trace[tid == 0 ? kTrNcPushed : kTrNcReduced] = global_ns();
@@ -1054,6 +1088,7 @@ void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const a
     a.pair_w = pair_w->data_ptr<float>();
     a.PK = static_cast<int>(pair_pos->size(1));
   }
+  a.round = progress_round();
   const int G = static_cast<int>(grid);
   TORCH_CHECK(G >= 1 && G <= kMaxGrid && send_start.numel() >= static_cast<int64_t>(G) * hv.R,
               "combine must run on the grid of its dispatch");

@@ -106,6 +106,8 @@ class NvlinkEngine:
             return round((t[b] - t[a]) / 1e3, 2) if t[a] and t[b] else None
         return {'dispatch.scan': d(0, 1), 'dispatch.counts_in': d(0, 2), 'dispatch.notified': d(0, 3),
                 'dispatch.cta0_pushed': d(0, 4), 'dispatch.cta0_received': d(0, 5), 'dispatch.total': d(0, 6),
+                'dispatch.cta0_published': d(0, 7), 'combine.cta0_published': d(16, 20),
+                'dispatch.cta0_recv_wait': round(t[8] / 1e3, 2), 'combine.cta0_reduce_wait': round(t[21] / 1e3, 2),
                 'gap.dispatch_to_combine': d(6, 16), 'combine.cta0_pushed': d(16, 17),
                 'combine.cta0_reduced': d(16, 18), 'combine.total': d(16, 19),
                 'step.dispatch_to_combine_end': d(0, 19),
