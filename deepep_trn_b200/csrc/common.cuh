@@ -117,6 +117,15 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys64(const uint64_t* p) {
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+// GPU-scope relaxed load: the polling load of a word that a peer GPU writes over NVLink into
+// this GPU's memory (the write lands in this GPU's L2, which these loads read). Pollers use it
+// and finish with one system-scope acquire of the same word, so their spinning issues no
+// system-scope operations on an SM whose other warps are pushing and releasing.
+__device__ __forceinline__ uint64_t ld_relaxed_gpu64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }

@@ -77,18 +77,20 @@ __device__ __forceinline__ uint32_t row_mask(const bool* p, int R) {
 }
 
 // Bounded spin on a 64-bit (q << 32) | value word until its tag is q; returns the value
-// (or -1 after recording a timeout). Polls with relaxed loads and backs off, so spinning
-// threads do not flood the memory system the pushing warps of the same SM are using; the
-// final load is an acquire.
+// (or -1 after recording a timeout). Polls with GPU-scope relaxed loads and backs off, then
+// acquires the word once at system scope. Spinning with system-scope loads on an SM whose
+// other warps push rows over NVLink and release progress words stalled those releases by
+// milliseconds (measured on B200: a combine's progress words landed 1.4-2.2 ms after its
+// last row was stored); GPU-scope polling leaves them alone.
 __device__ __forceinline__ int64_t wait_tagged(const uint64_t* p, uint32_t q, const HeapView& hv, uint32_t code,
                                                uint32_t op, int peer) {
-  uint64_t v = ld_relaxed_sys64(p);
+  uint64_t v = ld_relaxed_gpu64(p);
   if (static_cast<uint32_t>(v >> 32) != q) {
     const uint64_t t0 = global_ns();
     uint32_t spins = 0;
     while (true) {
-      __nanosleep(64);
-      v = ld_relaxed_sys64(p);
+      __nanosleep(128);
+      v = ld_relaxed_gpu64(p);
       if (static_cast<uint32_t>(v >> 32) == q) break;
       if ((++spins & 15u) == 0u && (global_ns() - t0 > hv.timeout_ns || has_error(hv.status))) {
         report_error(hv.status, code, op, hv.rank, peer, q, static_cast<uint32_t>(v >> 32));
@@ -101,19 +103,19 @@ __device__ __forceinline__ int64_t wait_tagged(const uint64_t* p, uint32_t q, co
 }
 
 // Bounded wait until a tagged progress word reports at least `want` rows for op q (one
-// thread polls; same backoff and final acquire as wait_tagged). Returns the rows seen.
+// thread polls; same GPU-scope polling and final acquire as wait_tagged). Returns the rows seen.
 __device__ __forceinline__ int64_t wait_progress(const uint64_t* p, uint32_t q, int64_t want, const HeapView& hv,
                                                  uint32_t op, int peer) {
   auto ok = [&](uint64_t x) {
     return static_cast<uint32_t>(x >> 32) == q && static_cast<int64_t>(x & 0xffffffffu) >= want;
   };
-  uint64_t v = ld_relaxed_sys64(p);
+  uint64_t v = ld_relaxed_gpu64(p);
   if (!ok(v)) {
     const uint64_t t0 = global_ns();
     uint32_t spins = 0;
     while (true) {
-      __nanosleep(64);
-      v = ld_relaxed_sys64(p);
+      __nanosleep(128);
+      v = ld_relaxed_gpu64(p);
       if (ok(v)) break;
       if ((++spins & 15u) == 0u && (global_ns() - t0 > hv.timeout_ns || has_error(hv.status))) {
         report_error(hv.status, kTimeoutReady, op, hv.rank, peer, static_cast<uint32_t>(want),
@@ -887,10 +889,19 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
         continue;
       }
       // items of the round: for each source (rotated), rows [k0, k0 + RR) of its range
-      for (int it = pw; it < R * RR; it += kMovers) {
-        const int s = (me + 1 + it / RR) % R;
-        const int u = k0 + it % RR;
-        if (u >= s_cnt[s]) continue;  // (own rows have no count unless in pair mode)
+      for (int it = pw;; it += kMovers) {
+        int s = -1, u = 0, rem = it;
+        for (int k = 1; k <= R; ++k) {
+          const int ss = (me + k) % R;   // (own rows have no count unless in pair mode)
+          const int n = max(0, min(s_cnt[ss] - k0, RR));
+          if (rem < n) {
+            s = ss;
+            u = k0 + rem;
+            break;
+          }
+          rem -= n;
+        }
+        if (s < 0) break;
         const int64_t j = s_start[s] + u;
         const int64_t i = s_off[s] + j;
         uint8_t* dst = hv.base[s] + hv.L.inbox + (static_cast<int64_t>(me) * M + j) * IS;
