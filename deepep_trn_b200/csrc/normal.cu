@@ -11,23 +11,24 @@
 //      every CTA knows where its range starts in each destination's block, writes the
 //      token -> row map (token_pos) and tells each destination (first row, rows) of
 //      its range; CTA 0 publishes this rank's row totals to every destination.
-//   2. warps 0..6 push: each token row goes straight from x to every other rank that
+//   2. push (every warp): each token row goes straight from x to every other rank that
 //      owns one of its experts, 16-byte stores into that rank's inbox over NVLink
 //      (fp8 e4m3 + 1x128 scales quantised in registers on the way when asked), with
-//      the token's top-k ids, weights and index appended; after each round of tokens
-//      warp 7 publishes per destination how many rows of the CTA's range have landed.
-//   3. warps 8..15 receive: as soon as every source's total is in, CTA 0 publishes the
+//      the token's top-k ids, weights and index appended; then one thread per destination
+//      publishes that the CTA's range has landed (a system-scope release).
+//   3. receive (every warp): as soon as every source's total is in, CTA 0 publishes the
 //      receive size to the host; every CTA then copies, for each source s, the rows
-//      that s's CTA b pushed (as its progress word advances) from the inbox to recv_x
+//      that s's CTA b pushed (once its progress word is in) from the inbox to recv_x
 //      at recv_off[s] + row, with the metadata. Rows a rank keeps come from x directly.
-// Combine (nc_kernel), same grid and the same ranges: warps 0..7 of expert rank r push
-// the rows of source s's range b back into s's inbox (weights appended); warps 8..15 of
-// source s reduce the tokens of range b in fp32 as their rows land (own rows read from
-// x in place), add the optional bias and cast once.
+// Combine (nc_kernel), same grid and the same ranges: expert rank r's CTA b pushes the
+// rows of every source s's range b back into s's inbox (weights appended) and publishes;
+// then source s's CTA b reduces the tokens of range b in fp32 as their rows are in (own
+// rows read from x in place), adds the optional bias and casts once. The CTAs of a GPU
+// are not in step, so some push while others already receive.
 //
-// Ordering: payload stores, then a release store of the progress word at system scope
-// by the publishing thread after a barrier of the pushing warps; receivers acquire the
-// word before reading rows. A rank writes into a peer's inbox (and progress / info
+// Ordering: payload stores, a block barrier, then a system-scope fence and release store
+// of the progress word by one thread per destination; receivers poll the word with
+// GPU-scope loads and acquire it at system scope before reading rows. A rank writes into a peer's inbox (and progress / info
 // words) for op q only after that peer reported that it finished reading its inbox for
 // op q - 1 (inbox_free), which every rank sends at the end of its kernel. Every wait is
 // bounded by the buffer's timeout and reports into the host-mapped status page.
@@ -44,22 +45,15 @@ namespace {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
-constexpr int kPushWarps = 8;                     // warps [0, 8) send, [8, 16) receive / reduce
-constexpr int kRecvWarps = kWarps - kPushWarps;
-// Of the sending warps, the last only publishes progress: all eight meet on a named barrier
-// after each round, then the publisher releases that round's progress words while the
-// others push the next round, so a system-scope release overlaps a round of pushes.
-constexpr int kMovers = kPushWarps - 1;
-constexpr int kPublisher = kPushWarps - 1;
-constexpr int kDefaultRound = 2 * kMovers;        // tokens (dispatch) / rows per source (combine) per publication
-constexpr int kBarPush = 1, kBarRecv = 2;         // named barriers of the two warp groups
-
+// Each CTA first pushes (every warp), then publishes one progress word per destination,
+// then receives or reduces (every warp). Splitting the roles in time rather than across the
+// warps of an SM was measured to matter: while receiving warps of the same SM were active,
+// the system-scope release that follows a CTA's NVLink stores took 0.7-2.2 ms to complete
+// (B200, EP2); with the SM doing nothing else it completes as soon as the stores have landed,
+// and CTAs still overlap with one another (some push while others receive).
 __device__ __forceinline__ int32_t ldv_i32(const int32_t* p) { return *reinterpret_cast<const volatile int32_t*>(p); }
 __device__ __forceinline__ uint32_t ldv_u32(const uint32_t* p) {
   return *reinterpret_cast<const volatile uint32_t*>(p);
-}
-__device__ __forceinline__ void group_sync(int id, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 __device__ __forceinline__ int warp_sum(int v) {
@@ -193,18 +187,6 @@ __device__ __forceinline__ void acc8(float (&acc)[8], const int4& raw) {
   for (int i = 0; i < 8; ++i) acc[i] += static_cast<float>(h[i]);
 }
 
-// Tokens (dispatch) or rows per source (combine) between two progress publications of a
-// CTA: B200EP_PROGRESS_ROUND, default two per moving warp; a large value publishes once,
-// at the end of the CTA's pushes.
-int progress_round() {
-  static const int r = [] {
-    const char* v = getenv("B200EP_PROGRESS_ROUND");
-    const int n = v ? atoi(v) : 0;
-    return n > 0 ? n : kDefaultRound;
-  }();
-  return r;
-}
-
 }  // namespace
 
 // ============================================================================ dispatch
@@ -236,7 +218,6 @@ struct NdArgs {
   int T, H, K, E;
   uint64_t ticket;
   int pad_rows;           // fill the metadata of rows [N, capacity) (sync-free sizing)
-  int round;              // tokens per progress publication
 };
 
 // Push warp `pw` writes token t to every destination of `dmask`: payload, scales, ids,
@@ -370,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
   __shared__ int32_t s_wcnt[kWarps][B200EP_MAX_RANKS];
   __shared__ int64_t s_roff[B200EP_MAX_RANKS + 1];
   __shared__ int32_t s_rcount[B200EP_MAX_RANKS];  // rows each source sends this rank
-  __shared__ int32_t s_pos[kPushWarps][B200EP_MAX_RANKS];
+  __shared__ int32_t s_pos[kWarps][B200EP_MAX_RANKS];
 
   if (tid == 0) s_fail = 0;
   if (tid < R) s_cnt[tid] = 0;
@@ -470,217 +451,185 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
     }
   }
 
-  if (warp < kPushWarps) {
-    // ------------------------------------------------------------ push (warps 0..7)
-    const int pw = warp;
-    if (!fail0) {
-      if (pw != kPublisher) {
-        for (int rt = t0; rt < t1; rt += a.round) {
-          const int re = min(rt + a.round, t1);
-          for (int t = rt + pw; t < re; t += kMovers) {
-            uint32_t m = 0;
-            if (lane < R) {
-              const int32_t p = a.token_pos[static_cast<int64_t>(t) * R + lane];
-              s_pos[pw][lane] = p;
-              m = (p >= 0 && lane != me) ? 1u : 0u;
-            }
-            const uint32_t dmask = __ballot_sync(0xffffffffu, m);
-            __syncwarp();
-            if (dmask) push_token<T16>(a, t, dmask, s_pos[pw]);
-            __syncwarp();
-          }
-          group_sync(kBarPush, kPushWarps * 32);
-        }
-      } else {
-        // lane r < R: rows of my range pushed to destination r, released after each round
-        int32_t done = 0;
-        uint64_t* prog = lane < R ? hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b
-                                  : nullptr;
-        for (int rt = t0; rt < t1; rt += a.round) {
-          const int re = min(rt + a.round, t1);
-          group_sync(kBarPush, kPushWarps * 32);
-          if (lane < R && lane != me) {
-            for (int t = rt; t < re; ++t) done += a.token_pos[static_cast<int64_t>(t) * R + lane] >= 0 ? 1 : 0;
-            st_release_sys64(prog, (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(done));
-          }
-        }
-        // an empty range still tells every destination that it is complete
-        if (t1 <= t0 && lane < R && lane != me) st_release_sys64(prog, static_cast<uint64_t>(q) << 32);
-        if (b == 0 && lane == 0) ls->trace[kTrNdPublished] = global_ns();
+  // ---------------------------------------------------------------- push (every warp)
+  if (!fail0) {
+    for (int t = t0 + warp; t < t1; t += kWarps) {
+      uint32_t m = 0;
+      if (lane < R) {
+        const int32_t p = a.token_pos[static_cast<int64_t>(t) * R + lane];
+        s_pos[warp][lane] = p;
+        m = (p >= 0 && lane != me) ? 1u : 0u;
       }
-    }
-  } else {
-    // ------------------------------------------------------------ receive (warps 8..15)
-    const int rt = tid - kPushWarps * 32, rw = warp - kPushWarps;
-    __shared__ int s_rfail;
-    if (rt == 0) s_rfail = fail0 ? 1 : 0;
-    group_sync(kBarRecv, kRecvWarps * 32);
-    if (rt < R && !fail0) {
-      const int64_t c = wait_tagged(&hv.sig(me)->nd_cnt[rt], q, hv, kTimeoutReady, 1, rt);
-      const int64_t g = c < 0 ? -1 : wait_tagged(&hv.sig(me)->nd_grid[rt], q, hv, kTimeoutReady, 1, rt);
-      if (c < 0 || g < 0) {
-        s_rfail = 1;
-        s_rcount[rt] = 0;
-      } else {
-        if (g != G) report_error(hv.status, kBadInput, 1, me, rt, G, static_cast<uint32_t>(g));
-        s_rcount[rt] = static_cast<int32_t>(c);
-        if (g != G) s_rfail = 1;
-      }
-    }
-    group_sync(kBarRecv, kRecvWarps * 32);
-    if (rt == 0) {
-      int64_t off = 0;
-      for (int s = 0; s < R; ++s) {
-        s_roff[s] = off;
-        off += s_rfail ? 0 : s_rcount[s];
-      }
-      s_roff[R] = off;
-      if (off > a.capacity) {
-        report_error(hv.status, kCapacity, 2, me, -1, static_cast<uint32_t>(a.capacity), static_cast<uint32_t>(off));
-        s_rfail = 1;
-      }
-    }
-    group_sync(kBarRecv, kRecvWarps * 32);
-    const bool rfail = s_rfail != 0;
-    const int64_t N = rfail ? 0 : s_roff[R];
-    if (b == 0) {
-      // handle offsets and the host notify page
-      if (rt <= R) a.recv_off[rt] = rfail ? 0 : s_roff[rt];
-      HostPage* host = hv.host;
-      if (rt < R) host->notify.recv_counts[rt] = rfail ? 0 : s_rcount[rt];
-      const int EL = a.E / R;
-      for (int le = rt; le < EL && le < 1024; le += kRecvWarps * 32) {
-        int32_t sum = 0;
-        if (!rfail && a.nte)
-          for (int s = 0; s < R; ++s) sum += ldv_i32(hv.at<int32_t>(s, hv.L.nd_nte) + me * EL + le);
-        host->notify.per_expert[le] = sum;
-      }
-      if (rt == 0) {
-        ls->trace[kTrNdCounts] = global_ns();
-        host->notify.num_recv = N;
-      }
-      group_sync(kBarRecv, kRecvWarps * 32);
-      if (rt == 0) {
-        __threadfence_system();
-        st_release_sys64(const_cast<uint64_t*>(&host->notify.ticket), a.ticket);
-        ls->trace[kTrNdNotified] = global_ns();
-      }
-    }
-    if (!rfail) {
-      // rows this rank keeps: straight from x (or quantised from it) into their final place
-      {
-        const int64_t base = s_roff[me];
-        for (int t = t0 + rw; t < t1; t += kRecvWarps) {
-          const int32_t p = a.token_pos[static_cast<int64_t>(t) * R + me];
-          if (p < 0) continue;
-          const int64_t i = base + p;
-          const uint8_t* src = a.x + static_cast<int64_t>(t) * a.x_stride;
-          if (a.mode == 0) {
-            warp_copy(a.recv_x + i * P, src, P);
-          } else if (a.mode == 1) {
-            warp_copy(a.recv_x + i * P, src, P);
-            warp_copy(a.recv_scales + i * (H / 128), a.xs + static_cast<int64_t>(t) * a.xs_stride, S);
-          } else {
-            warp_quant_row<T16>(a.recv_x + i * P, a.recv_scales + i * (H / 128),
-                                reinterpret_cast<const T16*>(src), H, a.round_scale);
-          }
-          // metadata from the caller's arrays
-          if (lane == 0) {
-            if (a.recv_src_i32)
-              static_cast<int32_t*>(a.recv_src)[i] = t;
-            else
-              static_cast<int64_t*>(a.recv_src)[i] = t;
-          }
-          if (a.recv_topk && lane < K) {
-            const int EL = a.E / R, lo = me * EL;
-            const int64_t k = static_cast<int64_t>(t) * K + lane;
-            const int32_t g = a.topk_i32 ? static_cast<const int32_t*>(a.topk)[k]
-                                         : static_cast<int32_t>(static_cast<const int64_t*>(a.topk)[k]);
-            const bool local = g >= lo && g < lo + EL;
-            const int64_t o = i * K + lane;
-            if (a.recv_topk_i32)
-              static_cast<int32_t*>(a.recv_topk)[o] = local ? g - lo : -1;
-            else
-              static_cast<int64_t*>(a.recv_topk)[o] = local ? g - lo : -1;
-            if (a.recv_w) a.recv_w[o] = local && a.topk_w ? a.topk_w[k] : 0.f;
-          }
-        }
-      }
-      uint64_t waited = 0;  // ns this warp spent waiting for progress words (CTA 0 reports it)
-      // rows pushed by other ranks: for each source (rotated), the rows of its CTA b's range
-      for (int k = 1; k < R && !rfail; ++k) {
-        const int s = (me + R - k) % R;
-        const uint64_t* info = hv.at<uint64_t>(me, hv.L.info) + (static_cast<int64_t>(s) * kMaxGrid + b) * 2;
-        __shared__ int64_t s_info[2];
-        if (rt == 0) {
-          const int64_t c = wait_tagged(info + 1, q, hv, kTimeoutReady, 1, s);
-          s_info[1] = c;
-          s_info[0] = c < 0 ? 0 : static_cast<int64_t>(ld_acquire_sys64(info) & 0xffffffffu);
-          if (c < 0) s_rfail = 1;
-        }
-        group_sync(kBarRecv, kRecvWarps * 32);
-        if (s_rfail) break;
-        const int64_t start = s_info[0], cnt = s_info[1];
-        if (rt == 0) {
-          a.recv_info[(static_cast<int64_t>(s) * kMaxGrid + b) * 2] = static_cast<int32_t>(start);
-          a.recv_info[(static_cast<int64_t>(s) * kMaxGrid + b) * 2 + 1] = static_cast<int32_t>(cnt);
-        }
-        const uint64_t* prog = hv.at<uint64_t>(me, hv.L.prog) + static_cast<int64_t>(s) * kMaxGrid + b;
-        int64_t seen = 0;
-        const uint8_t* blk = hv.at<uint8_t>(me, hv.L.inbox) + static_cast<int64_t>(s) * M * IS;
-        for (int64_t u = rw; u < cnt; u += kRecvWarps) {
-          if (u >= seen) {
-            // one lane polls; __syncwarp orders the other lanes' reads of the rows after its acquire
-            int64_t v = 0;
-            const uint64_t tw = global_ns();
-            if (lane == 0) v = wait_progress(prog, q, u + 1, hv, 1, s);
-            waited += global_ns() - tw;
-            seen = __shfl_sync(0xffffffffu, v, 0);
-            __syncwarp();
-            if (seen < 0) {
-              if (lane == 0) s_rfail = 1;
-              break;
-            }
-          }
-          const int64_t j = start + u;
-          const uint8_t* row = blk + j * IS;
-          const int64_t i = s_roff[s] + j;
-          warp_copy(a.recv_x + i * P, row, P);
-          if (S) warp_copy(a.recv_scales + i * (H / 128), row + P, S);
-          const int32_t* ids = reinterpret_cast<const int32_t*>(row + P + S);
-          const float* wts = reinterpret_cast<const float*>(row + P + S + 4 * K);
-          const int t = *reinterpret_cast<const int32_t*>(row + P + S + 8 * K);
-          emit_meta(a, i, t, ids, wts);
-        }
-        group_sync(kBarRecv, kRecvWarps * 32);
-      }
-      if (rt == 0 && s_rfail) report_error(hv.status, kTimeoutReady, 1, me, -1, 0, 0, 3);
-      if (b == 0 && lane == 0)
-        atomicAdd(reinterpret_cast<unsigned long long*>(&ls->trace[kTrNdWaitNs]),
-                  static_cast<unsigned long long>(waited / kRecvWarps));
-    }
-    // sync-free sizing: the rows past N carry no expert (-1), weight 0 and source -1
-    if (a.pad_rows) {
-      const int64_t n0 = N;
-      for (int64_t i = n0 + static_cast<int64_t>(b) * kRecvWarps * 32 + rt; i < a.capacity;
-           i += static_cast<int64_t>(G) * kRecvWarps * 32) {
-        if (a.recv_src_i32)
-          static_cast<int32_t*>(a.recv_src)[i] = -1;
-        else
-          static_cast<int64_t*>(a.recv_src)[i] = -1;
-        if (a.recv_topk)
-          for (int k = 0; k < K; ++k) {
-            if (a.recv_topk_i32)
-              static_cast<int32_t*>(a.recv_topk)[i * K + k] = -1;
-            else
-              static_cast<int64_t*>(a.recv_topk)[i * K + k] = -1;
-            if (a.recv_w) a.recv_w[i * K + k] = 0.f;
-          }
-      }
+      const uint32_t dmask = __ballot_sync(0xffffffffu, m);
+      __syncwarp();
+      if (dmask) push_token<T16>(a, t, dmask, s_pos[warp]);
+      __syncwarp();
     }
   }
-  if (b == 0 && (tid == 0 || tid == kPushWarps * 32))
-    ls->trace[tid == 0 ? kTrNdPushed : kTrNdRecvd] = global_ns();
+  __syncthreads();
+  if (b == 0 && tid == 0) ls->trace[kTrNdPushed] = global_ns();
+  // one release per destination covers every row of this CTA's range (an empty range too)
+  if (!fail0 && tid < R && tid != me) {
+    fence_sys();
+    st_release_sys64(hv.at<uint64_t>(tid, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
+                     (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(s_cnt[tid]));
+  }
+  if (b == 0 && tid == 0) ls->trace[kTrNdPublished] = global_ns();
+
+  // ---------------------------------------------------------------- receive (every warp)
+  __shared__ int s_rfail;
+  if (tid == 0) s_rfail = fail0 ? 1 : 0;
+  __syncthreads();
+  if (tid < R && !fail0) {
+    const int64_t c = wait_tagged(&hv.sig(me)->nd_cnt[tid], q, hv, kTimeoutReady, 1, tid);
+    const int64_t g = c < 0 ? -1 : wait_tagged(&hv.sig(me)->nd_grid[tid], q, hv, kTimeoutReady, 1, tid);
+    if (c < 0 || g < 0) {
+      s_rfail = 1;
+      s_rcount[tid] = 0;
+    } else {
+      if (g != G) report_error(hv.status, kBadInput, 1, me, tid, G, static_cast<uint32_t>(g));
+      s_rcount[tid] = static_cast<int32_t>(c);
+      if (g != G) s_rfail = 1;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int64_t off = 0;
+    for (int s = 0; s < R; ++s) {
+      s_roff[s] = off;
+      off += s_rfail ? 0 : s_rcount[s];
+    }
+    s_roff[R] = off;
+    if (off > a.capacity) {
+      report_error(hv.status, kCapacity, 2, me, -1, static_cast<uint32_t>(a.capacity), static_cast<uint32_t>(off));
+      s_rfail = 1;
+    }
+  }
+  __syncthreads();
+  const bool rfail = s_rfail != 0;
+  const int64_t N = rfail ? 0 : s_roff[R];
+  if (b == 0) {
+    // handle offsets and the host notify page
+    if (tid <= R) a.recv_off[tid] = rfail ? 0 : s_roff[tid];
+    HostPage* host = hv.host;
+    if (tid < R) host->notify.recv_counts[tid] = rfail ? 0 : s_rcount[tid];
+    const int EL = a.E / R;
+    for (int le = tid; le < EL && le < 1024; le += kThreads) {
+      int32_t sum = 0;
+      if (!rfail && a.nte)
+        for (int s = 0; s < R; ++s) sum += ldv_i32(hv.at<int32_t>(s, hv.L.nd_nte) + me * EL + le);
+      host->notify.per_expert[le] = sum;
+    }
+    if (tid == 0) {
+      ls->trace[kTrNdCounts] = global_ns();
+      host->notify.num_recv = N;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence_system();
+      st_release_sys64(const_cast<uint64_t*>(&host->notify.ticket), a.ticket);
+      ls->trace[kTrNdNotified] = global_ns();
+    }
+  }
+  if (!rfail) {
+    // rows this rank keeps: straight from x (or quantised from it) into their final place
+    const int64_t base = s_roff[me];
+    for (int t = t0 + warp; t < t1; t += kWarps) {
+      const int32_t p = a.token_pos[static_cast<int64_t>(t) * R + me];
+      if (p < 0) continue;
+      const int64_t i = base + p;
+      const uint8_t* src = a.x + static_cast<int64_t>(t) * a.x_stride;
+      if (a.mode == 0) {
+        warp_copy(a.recv_x + i * P, src, P);
+      } else if (a.mode == 1) {
+        warp_copy(a.recv_x + i * P, src, P);
+        warp_copy(a.recv_scales + i * (H / 128), a.xs + static_cast<int64_t>(t) * a.xs_stride, S);
+      } else {
+        warp_quant_row<T16>(a.recv_x + i * P, a.recv_scales + i * (H / 128), reinterpret_cast<const T16*>(src), H,
+                            a.round_scale);
+      }
+      // metadata from the caller's arrays
+      if (lane == 0) {
+        if (a.recv_src_i32)
+          static_cast<int32_t*>(a.recv_src)[i] = t;
+        else
+          static_cast<int64_t*>(a.recv_src)[i] = t;
+      }
+      if (a.recv_topk && lane < K) {
+        const int EL = a.E / R, lo = me * EL;
+        const int64_t k = static_cast<int64_t>(t) * K + lane;
+        const int32_t g = a.topk_i32 ? static_cast<const int32_t*>(a.topk)[k]
+                                     : static_cast<int32_t>(static_cast<const int64_t*>(a.topk)[k]);
+        const bool local = g >= lo && g < lo + EL;
+        const int64_t o = i * K + lane;
+        if (a.recv_topk_i32)
+          static_cast<int32_t*>(a.recv_topk)[o] = local ? g - lo : -1;
+        else
+          static_cast<int64_t*>(a.recv_topk)[o] = local ? g - lo : -1;
+        if (a.recv_w) a.recv_w[o] = local && a.topk_w ? a.topk_w[k] : 0.f;
+      }
+    }
+    uint64_t waited = 0;  // ns this warp spent waiting for progress words (CTA 0 reports it)
+    // rows pushed by other ranks: for each source (rotated), the rows of its CTA b's range
+    for (int k = 1; k < R; ++k) {
+      const int s = (me + R - k) % R;
+      const uint64_t* info = hv.at<uint64_t>(me, hv.L.info) + (static_cast<int64_t>(s) * kMaxGrid + b) * 2;
+      __shared__ int64_t s_info[2];
+      if (tid == 0) {
+        const uint64_t tw = global_ns();
+        const int64_t c = wait_tagged(info + 1, q, hv, kTimeoutReady, 1, s);
+        s_info[1] = c;
+        s_info[0] = c < 0 ? 0 : static_cast<int64_t>(ld_acquire_sys64(info) & 0xffffffffu);
+        if (c < 0) s_rfail = 1;
+        // the whole range lands before its one progress word
+        if (c > 0 && wait_progress(hv.at<uint64_t>(me, hv.L.prog) + static_cast<int64_t>(s) * kMaxGrid + b, q, c,
+                                   hv, 1, s) < 0)
+          s_rfail = 1;
+        waited += global_ns() - tw;
+      }
+      __syncthreads();  // every thread reads rows that thread 0 acquired
+      if (s_rfail) break;
+      const int64_t start = s_info[0], cnt = s_info[1];
+      if (tid == 0) {
+        a.recv_info[(static_cast<int64_t>(s) * kMaxGrid + b) * 2] = static_cast<int32_t>(start);
+        a.recv_info[(static_cast<int64_t>(s) * kMaxGrid + b) * 2 + 1] = static_cast<int32_t>(cnt);
+      }
+      const uint8_t* blk = hv.at<uint8_t>(me, hv.L.inbox) + static_cast<int64_t>(s) * M * IS;
+      for (int64_t u = warp; u < cnt; u += kWarps) {
+        const int64_t j = start + u;
+        const uint8_t* row = blk + j * IS;
+        const int64_t i = s_roff[s] + j;
+        warp_copy(a.recv_x + i * P, row, P);
+        if (S) warp_copy(a.recv_scales + i * (H / 128), row + P, S);
+        const int32_t* ids = reinterpret_cast<const int32_t*>(row + P + S);
+        const float* wts = reinterpret_cast<const float*>(row + P + S + 4 * K);
+        const int t = *reinterpret_cast<const int32_t*>(row + P + S + 8 * K);
+        emit_meta(a, i, t, ids, wts);
+      }
+      __syncthreads();
+    }
+    if (tid == 0 && s_rfail) report_error(hv.status, kTimeoutReady, 1, me, -1, 0, 0, 3);
+    if (b == 0 && tid == 0) ls->trace[kTrNdWaitNs] = waited;
+  }
+  // sync-free sizing: the rows past N carry no expert (-1), weight 0 and source -1
+  if (a.pad_rows) {
+    for (int64_t i = N + static_cast<int64_t>(b) * kThreads + tid; i < a.capacity;
+         i += static_cast<int64_t>(G) * kThreads) {
+      if (a.recv_src_i32)
+        static_cast<int32_t*>(a.recv_src)[i] = -1;
+      else
+        static_cast<int64_t*>(a.recv_src)[i] = -1;
+      if (a.recv_topk)
+        for (int k = 0; k < K; ++k) {
+          if (a.recv_topk_i32)
+            static_cast<int32_t*>(a.recv_topk)[i * K + k] = -1;
+          else
+            static_cast<int64_t*>(a.recv_topk)[i * K + k] = -1;
+          if (a.recv_w) a.recv_w[i * K + k] = 0.f;
+        }
+    }
+  }
+  if (b == 0 && tid == 0) ls->trace[kTrNdRecvd] = global_ns();
   __syncthreads();
   finish_op(ls, hv, q, kTrNdEnd);
 }
@@ -766,7 +715,6 @@ void nd_dispatch(SymmHeap& heap, const at::Tensor& x, const OptTensor& x_scales,
   a.recv_src = recv_src.data_ptr();
   a.recv_src_i32 = recv_src.scalar_type() == at::kInt;
   a.pad_rows = pad_rows ? 1 : 0;
-  a.round = progress_round();
   void* fn = a.x_fp16 ? reinterpret_cast<void*>(nd_kernel<__half>) : reinterpret_cast<void*>(nd_kernel<__nv_bfloat16>);
   void* args[] = {&a};
   // cooperative: CTAs wait for one another (grid barrier) and for peers' CTAs, so all must be resident
@@ -796,7 +744,6 @@ struct NcArgs {
   const int32_t* pair_pos;  // [N, PK], -1 = no pair
   const float* pair_w;      // [N, PK]
   int PK;
-  int round;                // rows per source per progress publication
 };
 
 // Pair mode: one warp forms row i = sum_k w[i, k] * pairs[pos[i, k]] in fp32 (k ascending) and
@@ -873,65 +820,56 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
   __syncthreads();
   const bool fail0 = s_fail != 0;
 
-  if (warp < kPushWarps) {
-    // ------------------------------------------------------------ push rows home (warps 0..7)
-    const int pw = warp;
-    int32_t maxc = 0;
-    for (int s = 0; s < R; ++s) maxc = max(maxc, s_cnt[s]);
-    const int RR = a.round;
-    for (int k0 = 0; k0 < maxc && !fail0; k0 += RR) {
-      if (pw == kPublisher) {
-        // release the round's progress once the moving warps have met here
-        group_sync(kBarPush, kPushWarps * 32);
-        if (lane < R && s_cnt[lane] > 0)
-          st_release_sys64(hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
-                           (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(min(s_cnt[lane], k0 + RR)));
-        continue;
-      }
-      // items of the round: for each source (rotated), rows [k0, k0 + RR) of its range
-      for (int it = pw;; it += kMovers) {
-        int s = -1, u = 0, rem = it;
-        for (int k = 1; k <= R; ++k) {
-          const int ss = (me + k) % R;   // (own rows have no count unless in pair mode)
-          const int n = max(0, min(s_cnt[ss] - k0, RR));
-          if (rem < n) {
-            s = ss;
-            u = k0 + rem;
-            break;
-          }
-          rem -= n;
+  // ---------------------------------------------------------------- push rows home (every warp)
+  if (!fail0) {
+    // rows of every source's range, the sources rotated per CTA so the CTAs of a rank spread
+    // their stores over all peers at once
+    for (int it = warp;; it += kWarps) {
+      int s = -1, u = 0, rem = it;
+      for (int k = 1; k <= R; ++k) {
+        const int ss = (me + b + k) % R;   // (own rows have no count unless in pair mode)
+        if (rem < s_cnt[ss]) {
+          s = ss;
+          u = rem;
+          break;
         }
-        if (s < 0) break;
-        const int64_t j = s_start[s] + u;
-        const int64_t i = s_off[s] + j;
-        uint8_t* dst = hv.base[s] + hv.L.inbox + (static_cast<int64_t>(me) * M + j) * IS;
-        if (a.pairs)
-          push_pair_row<T16>(a, i, dst);
-        else
-          warp_copy(dst, a.x + i * a.x_stride, RB);
-        if (a.has_w && lane < K) reinterpret_cast<float*>(dst + RB)[lane] = a.w[i * a.w_stride + lane];
+        rem -= s_cnt[ss];
       }
-      group_sync(kBarPush, kPushWarps * 32);
+      if (s < 0) break;
+      const int64_t j = s_start[s] + u;
+      const int64_t i = s_off[s] + j;
+      uint8_t* dst = hv.base[s] + hv.L.inbox + (static_cast<int64_t>(me) * M + j) * IS;
+      if (a.pairs)
+        push_pair_row<T16>(a, i, dst);
+      else
+        warp_copy(dst, a.x + i * a.x_stride, RB);
+      if (a.has_w && lane < K) reinterpret_cast<float*>(dst + RB)[lane] = a.w[i * a.w_stride + lane];
     }
-    if (pw == kPublisher && lane < R && (lane != me || a.pairs) && s_cnt[lane] == 0 && !fail0)
-      st_release_sys64(hv.at<uint64_t>(lane, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
-                       static_cast<uint64_t>(q) << 32);
-    if (pw == kPublisher && b == 0 && lane == 0) ls->trace[kTrNcPublished] = global_ns();
-  } else {
-    // ------------------------------------------------------------ reduce my tokens (warps 8..15)
-    const int rw = warp - kPushWarps;
+  }
+  __syncthreads();
+  if (b == 0 && tid == 0) ls->trace[kTrNcPushed] = global_ns();
+  // one release per source covers every row of its range (an empty range too)
+  if (!fail0 && tid < R && (tid != me || a.pairs)) {
+    fence_sys();
+    st_release_sys64(hv.at<uint64_t>(tid, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
+                     (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(s_cnt[tid]));
+  }
+  if (b == 0 && tid == 0) ls->trace[kTrNcPublished] = global_ns();
+  {
+    // ------------------------------------------------------------ reduce my tokens (every warp)
+    const int rw = warp;
     const int t0 = static_cast<int>(static_cast<int64_t>(a.T) * b / G);
     const int t1 = static_cast<int>(static_cast<int64_t>(a.T) * (b + 1) / G);
-    __shared__ int64_t s_seen[kRecvWarps][B200EP_MAX_RANKS];
-    __shared__ const uint8_t* s_rows[kRecvWarps][B200EP_MAX_RANKS];
-    __shared__ const float* s_wrows[kRecvWarps][B200EP_MAX_RANKS];
+    __shared__ int64_t s_seen[kWarps][B200EP_MAX_RANKS];
+    __shared__ const uint8_t* s_rows[kWarps][B200EP_MAX_RANKS];
+    __shared__ const float* s_wrows[kWarps][B200EP_MAX_RANKS];
     if (lane < R) s_seen[rw][lane] = 0;
     __syncwarp();
     const uint8_t* inbox = hv.at<uint8_t>(me, hv.L.inbox);
     const int nch = H / 8;
     bool wfail = fail0;
     uint64_t waited = 0;   // ns this lane spent waiting for progress words (CTA 0 reports it)
-    for (int t = t0 + rw; t < t1 && !wfail; t += kRecvWarps) {
+    for (int t = t0 + rw; t < t1 && !wfail; t += kWarps) {
       // this token's rows: one per rank that received it
       int32_t pos = lane < R ? a.token_pos[static_cast<int64_t>(t) * R + lane] : -1;
       const uint8_t* rp = nullptr;
@@ -1036,12 +974,11 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
       // mean wait per reducing warp (the slowest lane of each warp), for the device trace
       for (int m = 16; m >= 1; m >>= 1) waited = max(waited, __shfl_xor_sync(0xffffffffu, waited, m));
       if (lane == 0) atomicAdd(reinterpret_cast<unsigned long long*>(&ls->trace[kTrNcWaitNs]),
-                               static_cast<unsigned long long>(waited / kRecvWarps));
+                               static_cast<unsigned long long>(waited / kWarps));
     }
   }
-  if (b == 0 && (tid == 0 || tid == kPushWarps * 32))
-    ls->trace[tid == 0 ? kTrNcPushed : kTrNcReduced] = global_ns();
   __syncthreads();
+  if (b == 0 && tid == 0) ls->trace[kTrNcReduced] = global_ns();
   finish_op(ls, hv, q, kTrNcEnd);
 }
 
@@ -1099,7 +1036,6 @@ void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const a
     a.pair_w = pair_w->data_ptr<float>();
     a.PK = static_cast<int>(pair_pos->size(1));
   }
-  a.round = progress_round();
   const int G = static_cast<int>(grid);
   TORCH_CHECK(G >= 1 && G <= kMaxGrid && send_start.numel() >= static_cast<int64_t>(G) * hv.R,
               "combine must run on the grid of its dispatch");
