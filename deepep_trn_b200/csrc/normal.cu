@@ -754,7 +754,9 @@ __device__ void push_pair_row(const NcArgs& a, int64_t i, uint8_t* dst) {
   const int32_t mp = lane < PK ? a.pair_pos[i * PK + lane] : -1;
   const float mw = lane < PK ? a.pair_w[i * PK + lane] : 0.f;
   constexpr int U = 4;
-  for (int c0 = lane; c0 < nch; c0 += 32 * U) {
+  // the loop bounds are warp-uniform (every lane takes part in the shuffles)
+  for (int base = 0; base < nch; base += 32 * U) {
+    const int c0 = base + lane;
     float acc[U][8];
 #pragma unroll
     for (int u = 0; u < U; ++u)
@@ -855,48 +857,49 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
                      (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(s_cnt[tid]));
   }
   if (b == 0 && tid == 0) ls->trace[kTrNcPublished] = global_ns();
+  // ---------------------------------------------------------------- wait for this range's rows
+  // One thread per rank polls that rank's progress word for range b (one word per range, so its
+  // tag alone says the range has landed). Keeping the pollers few matters: a few thousand
+  // threads polling the same few lines of L2 slowed the NVLink writes arriving at this GPU
+  // to a trickle (B200, EP2).
+  __shared__ int s_wfail;
+  if (tid == 0) s_wfail = fail0 ? 1 : 0;
+  __syncthreads();
+  uint64_t waited = 0;
+  if (!fail0 && tid < R && (tid != me || a.pairs)) {
+    const uint64_t tw = global_ns();
+    if (wait_tagged(hv.at<uint64_t>(me, hv.L.prog) + static_cast<int64_t>(tid) * kMaxGrid + b, q, hv,
+                    kTimeoutCombine, 3, tid) < 0)
+      s_wfail = 1;
+    waited = global_ns() - tw;
+  }
+  __syncthreads();  // every thread reads rows that the pollers acquired
+  if (b == 0 && tid < R) atomicMax(reinterpret_cast<unsigned long long*>(&ls->trace[kTrNcWaitNs]),
+                                   static_cast<unsigned long long>(waited));
   {
     // ------------------------------------------------------------ reduce my tokens (every warp)
     const int rw = warp;
     const int t0 = static_cast<int>(static_cast<int64_t>(a.T) * b / G);
     const int t1 = static_cast<int>(static_cast<int64_t>(a.T) * (b + 1) / G);
-    __shared__ int64_t s_seen[kWarps][B200EP_MAX_RANKS];
     __shared__ const uint8_t* s_rows[kWarps][B200EP_MAX_RANKS];
     __shared__ const float* s_wrows[kWarps][B200EP_MAX_RANKS];
-    if (lane < R) s_seen[rw][lane] = 0;
-    __syncwarp();
     const uint8_t* inbox = hv.at<uint8_t>(me, hv.L.inbox);
     const int nch = H / 8;
-    bool wfail = fail0;
-    uint64_t waited = 0;   // ns this lane spent waiting for progress words (CTA 0 reports it)
+    const bool wfail = s_wfail != 0;
     for (int t = t0 + rw; t < t1 && !wfail; t += kWarps) {
       // this token's rows: one per rank that received it
       int32_t pos = lane < R ? a.token_pos[static_cast<int64_t>(t) * R + lane] : -1;
       const uint8_t* rp = nullptr;
       const float* wp = nullptr;
-      bool bad = false;
       if (pos >= 0) {
         if (lane == me && !a.pairs) {
           const int64_t i = s_off[me] + pos;
           rp = a.x + i * a.x_stride;
           wp = a.has_w ? a.w + i * a.w_stride : nullptr;
         } else {
-          const int64_t want = pos - a.send_start[b * R + lane] + 1;
-          if (want > s_seen[rw][lane]) {
-            const uint64_t tw = global_ns();
-            const int64_t v = wait_progress(hv.at<uint64_t>(me, hv.L.prog) + static_cast<int64_t>(lane) * kMaxGrid + b,
-                                            q, want, hv, 3, lane);
-            waited += global_ns() - tw;
-            if (v < 0) bad = true; else s_seen[rw][lane] = v;
-          }
           rp = inbox + (static_cast<int64_t>(lane) * M + pos) * IS;
           wp = a.has_w ? reinterpret_cast<const float*>(rp + RB) : nullptr;
         }
-      }
-      __syncwarp();  // every lane reads every row: order those reads after each lane's acquire
-      if (__any_sync(0xffffffffu, bad)) {
-        wfail = true;
-        break;
       }
       const uint32_t have = __ballot_sync(0xffffffffu, pos >= 0);
       const int nr = __popc(have);
@@ -968,13 +971,6 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
         a.out_w[static_cast<int64_t>(t) * K + lane] = sw;
       }
       __syncwarp();
-    }
-    if (wfail && lane == 0) report_error(hv.status, kTimeoutCombine, 3, me, -1, 0, 0, 2);
-    if (b == 0) {
-      // mean wait per reducing warp (the slowest lane of each warp), for the device trace
-      for (int m = 16; m >= 1; m >>= 1) waited = max(waited, __shfl_xor_sync(0xffffffffu, waited, m));
-      if (lane == 0) atomicAdd(reinterpret_cast<unsigned long long*>(&ls->trace[kTrNcWaitNs]),
-                               static_cast<unsigned long long>(waited / kWarps));
     }
   }
   __syncthreads();
