@@ -107,6 +107,11 @@ __device__ __forceinline__ uint64_t ld_acquire_sys64(const uint64_t* p) {
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -159,26 +164,32 @@ __device__ __forceinline__ bool epoch_reached(uint32_t seen, uint32_t want) {
 }
 
 // Spin until *flag reaches `want` or the budget runs out. Returns false on timeout
-// (after recording it); callers then skip their work and return.
+// (after recording it); callers then skip their work and return. Polls with GPU-scope loads
+// and a short back-off and acquires the flag once at system scope: many threads spinning with
+// system-scope loads on a few lines of L2 were measured to slow the NVLink writes arriving at
+// the GPU.
 __device__ __forceinline__ bool wait_epoch(const uint32_t* flag, uint32_t want, uint64_t budget_ns, Status* st,
                                            uint32_t code, uint32_t op, int rank, int peer,
                                            uint64_t* waited_ns = nullptr) {
-  uint32_t v = ld_acquire_sys(flag);
-  if (epoch_reached(v, want)) return true;
-  const uint64_t t0 = global_ns();
-  uint32_t spins = 0;
-  while (true) {
-    v = ld_acquire_sys(flag);
-    if (epoch_reached(v, want)) break;
-    if ((++spins & 63u) == 0u) {
-      const uint64_t dt = global_ns() - t0;
-      if (dt > budget_ns || has_error(st)) {
-        report_error(st, code, op, rank, peer, want, v);
-        return false;
+  uint32_t v = ld_relaxed_gpu(flag);
+  if (!epoch_reached(v, want)) {
+    const uint64_t t0 = global_ns();
+    uint32_t spins = 0;
+    while (true) {
+      __nanosleep(32);
+      v = ld_relaxed_gpu(flag);
+      if (epoch_reached(v, want)) break;
+      if ((++spins & 31u) == 0u) {
+        const uint64_t dt = global_ns() - t0;
+        if (dt > budget_ns || has_error(st)) {
+          report_error(st, code, op, rank, peer, want, v);
+          return false;
+        }
       }
     }
+    if (waited_ns) *waited_ns += global_ns() - t0;
   }
-  if (waited_ns) *waited_ns += global_ns() - t0;
+  (void)ld_acquire_sys(flag);
   return true;
 }
 
