@@ -262,7 +262,7 @@ def main():
     if not args.no_ll and args.impl in ('ours', 'nccl'):
         ll = bench_ll(args, buf, rank, dev, control, graph=args.impl == 'ours')
         if args.trace and args.impl == 'ours':
-            tr = {k: v for k, v in buf.device_trace().items() if k.startswith('ll.')}
+            tr = ll.pop('_trace', None) or {}
             everyone = [None] * world
             dist.all_gather_object(everyone, (rank, tr), group=control)
             if rank == 0:
@@ -402,8 +402,11 @@ def bench_ll(args, buf, rank, dev, control, graph: bool = True, hook: bool = Tru
     dist.barrier(group=control)
     us = max_over_ranks(_events_us(gr.replay, 50))
     del gr
+    trace = {k: v for k, v in buf.device_trace().items() if k.startswith('ll.')} if args.trace else None
     res = {'tokens_per_rank': T, 'dispatch_fp8_plus_combine_us': round(us, 2), 'cuda_graph': True,
            'launches_per_iter': 4, 'check': check}
+    if trace is not None:
+        res['_trace'] = trace   # phase stamps of the last plain replay (printed, not reported)
     if hook:
         a = torch.randn(2048, H, generator=g).to(torch.bfloat16).to(dev)
         b = torch.randn(H, H, generator=g).to(torch.bfloat16).to(dev) * 0.01

@@ -164,20 +164,19 @@ __device__ __forceinline__ bool epoch_reached(uint32_t seen, uint32_t want) {
 }
 
 // Spin until *flag reaches `want` or the budget runs out. Returns false on timeout
-// (after recording it); callers then skip their work and return. Polls with GPU-scope loads
-// and a short back-off and acquires the flag once at system scope: many threads spinning with
-// system-scope loads on a few lines of L2 were measured to slow the NVLink writes arriving at
-// the GPU.
+// (after recording it); callers then skip their work and return. Flags are written by other
+// GPUs, so they are polled with system-scope relaxed loads (a GPU-scope load need not observe
+// a peer's store), with a short back-off between polls, and acquired once at system scope.
 __device__ __forceinline__ bool wait_epoch(const uint32_t* flag, uint32_t want, uint64_t budget_ns, Status* st,
                                            uint32_t code, uint32_t op, int rank, int peer,
                                            uint64_t* waited_ns = nullptr) {
-  uint32_t v = ld_relaxed_gpu(flag);
+  uint32_t v = ld_relaxed_sys(flag);
   if (!epoch_reached(v, want)) {
     const uint64_t t0 = global_ns();
     uint32_t spins = 0;
     while (true) {
       __nanosleep(32);
-      v = ld_relaxed_gpu(flag);
+      v = ld_relaxed_sys(flag);
       if (epoch_reached(v, want)) break;
       if ((++spins & 31u) == 0u) {
         const uint64_t dt = global_ns() - t0;

@@ -81,7 +81,7 @@ struct HeapConfig {
 
 struct HeapLayout {
   int64_t sig, local;
-  int64_t row_stride;      // bytes per low-latency row: align16(2H); fp8 rows use [H payload | H/32 scales]
+  int64_t row_stride;      // bytes per low-latency row: 2H rounded up to 128; fp8 rows use [H payload | H/32 scales]
   int64_t inbox_stride;    // bytes per inbox row: payload, scales, top-k ids and weights, source token
   int64_t inbox;           // [R][M] rows of inbox_stride bytes
   int64_t nd_nte;          // [E] int32: this rank's tokens per expert (read by peers)
@@ -99,7 +99,10 @@ __host__ __device__ inline int64_t align_up(int64_t v, int64_t a) { return (v + 
 
 // Inbox row: [payload: 2H (16-bit) or H (fp8) | fp8 scales: H/32 | ids: 4K | weights: 4K | token: 4]
 // for dispatch, [payload: 2H | weights: 4K] for combine; the 16-bit dispatch row is the longest.
-__host__ __device__ inline int64_t inbox_row_bytes(int64_t H, int64_t K) { return align_up(2 * H + 8 * K + 4, 16); }
+// Rows start on 128-byte lines, so a warp's 512-byte run of 16-byte stores covers whole lines
+// (a run that starts mid-line leaves partly written 32-byte sectors at both ends, each one a
+// masked write over NVLink).
+__host__ __device__ inline int64_t inbox_row_bytes(int64_t H, int64_t K) { return align_up(2 * H + 8 * K + 4, 128); }
 
 // Every region is followed by a 256-byte guard zone that the host fills with kCanaryByte at
 // construction and checks on request (SymmHeap::check_canaries): a kernel that writes past
@@ -121,7 +124,7 @@ inline HeapLayout make_layout(const HeapConfig& c, int64_t* guards = nullptr, in
   };
   L.sig = take(sizeof(Signals));
   L.local = take(sizeof(LocalState));
-  L.row_stride = align_up(2LL * c.H, 16);
+  L.row_stride = align_up(2LL * c.H, 128);
   L.inbox_stride = inbox_row_bytes(c.H, c.K);
   L.inbox = take(int64_t(c.R) * c.M * L.inbox_stride);
   L.nd_nte = take(int64_t(c.E) * 4);

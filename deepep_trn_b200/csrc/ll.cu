@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
   if (tid < R) {
     const uint64_t* hdr = &hv.sig(me)->ll_hdr[slot][tid];
     const uint64_t t0 = global_ns();
-    uint64_t v = ld_relaxed_gpu64(hdr);
+    uint64_t v = ld_relaxed_sys64(hdr);
     uint32_t spins = 0;
     while (!epoch_reached(static_cast<uint32_t>(v >> 32), e)) {
       if ((++spins & 31u) == 0u && (global_ns() - t0 > hv.timeout_ns || has_error(hv.status))) {
@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
         break;
       }
       __nanosleep(32);
-      v = ld_relaxed_gpu64(hdr);
+      v = ld_relaxed_sys64(hdr);
     }
     if (!s_fail) v = ld_acquire_sys64(hdr);
     s_T[tid] = epoch_reached(static_cast<uint32_t>(v >> 32), e) ? static_cast<int>(v & 0xffffffffu) : 0;

@@ -71,20 +71,21 @@ __device__ __forceinline__ uint32_t row_mask(const bool* p, int R) {
 }
 
 // Bounded spin on a 64-bit (q << 32) | value word until its tag is q; returns the value
-// (or -1 after recording a timeout). Polls with GPU-scope relaxed loads and backs off, then
-// acquires the word once at system scope. Spinning with system-scope loads on an SM whose
-// other warps push rows over NVLink and release progress words stalled those releases by
-// milliseconds (measured on B200: a combine's progress words landed 1.4-2.2 ms after its
-// last row was stored); GPU-scope polling leaves them alone.
+// (or -1 after recording a timeout). The word is written by another GPU, so it is polled
+// with system-scope relaxed loads (a GPU-scope load need not observe a peer GPU's store: the
+// peer's thread is outside the .gpu scope), backing off between polls, and acquired once at
+// system scope when the tag matches. Callers keep the pollers few (one thread per peer and
+// CTA): thousands of threads polling a few L2 lines were measured to slow the NVLink writes
+// arriving at the GPU.
 __device__ __forceinline__ int64_t wait_tagged(const uint64_t* p, uint32_t q, const HeapView& hv, uint32_t code,
                                                uint32_t op, int peer) {
-  uint64_t v = ld_relaxed_gpu64(p);
+  uint64_t v = ld_relaxed_sys64(p);
   if (static_cast<uint32_t>(v >> 32) != q) {
     const uint64_t t0 = global_ns();
     uint32_t spins = 0;
     while (true) {
       __nanosleep(128);
-      v = ld_relaxed_gpu64(p);
+      v = ld_relaxed_sys64(p);
       if (static_cast<uint32_t>(v >> 32) == q) break;
       if ((++spins & 15u) == 0u && (global_ns() - t0 > hv.timeout_ns || has_error(hv.status))) {
         report_error(hv.status, code, op, hv.rank, peer, q, static_cast<uint32_t>(v >> 32));
@@ -97,19 +98,19 @@ __device__ __forceinline__ int64_t wait_tagged(const uint64_t* p, uint32_t q, co
 }
 
 // Bounded wait until a tagged progress word reports at least `want` rows for op q (one
-// thread polls; same GPU-scope polling and final acquire as wait_tagged). Returns the rows seen.
+// thread polls; same system-scope polling and final acquire as wait_tagged). Returns the rows seen.
 __device__ __forceinline__ int64_t wait_progress(const uint64_t* p, uint32_t q, int64_t want, const HeapView& hv,
                                                  uint32_t op, int peer) {
   auto ok = [&](uint64_t x) {
     return static_cast<uint32_t>(x >> 32) == q && static_cast<int64_t>(x & 0xffffffffu) >= want;
   };
-  uint64_t v = ld_relaxed_gpu64(p);
+  uint64_t v = ld_relaxed_sys64(p);
   if (!ok(v)) {
     const uint64_t t0 = global_ns();
     uint32_t spins = 0;
     while (true) {
       __nanosleep(128);
-      v = ld_relaxed_gpu64(p);
+      v = ld_relaxed_sys64(p);
       if (ok(v)) break;
       if ((++spins & 15u) == 0u && (global_ns() - t0 > hv.timeout_ns || has_error(hv.status))) {
         report_error(hv.status, kTimeoutReady, op, hv.rank, peer, static_cast<uint32_t>(want),

@@ -96,8 +96,9 @@ class NvlinkEngine:
             raise DeviceError(f'heap guard zones overwritten at byte offsets {bad} (rank {self.rank})')
 
     def device_trace(self) -> dict:
-        """Phase durations (us) of the last normal-mode dispatch / combine on this rank, from
-        %globaltimer stamps the kernels write into the heap (synchronises the device)."""
+        """Phase durations (us) of the last normal-mode dispatch / combine and low-latency round
+        on this rank, from %globaltimer stamps the kernels write into the heap (synchronises the
+        device); ``abs.*`` are the raw stamps in ns."""
         if self.heap is None:
             return {}
         t = self.heap.trace()
@@ -114,7 +115,10 @@ class NvlinkEngine:
                 'll.dispatch_send': d(24, 25), 'll.gap_send_to_recv': d(25, 26), 'll.dispatch_recv_wait': d(26, 27),
                 'll.dispatch_recv_copy': d(27, 28), 'll.gap_to_combine': d(28, 32), 'll.combine_send': d(32, 33),
                 'll.gap_send_to_recv2': d(33, 34), 'll.combine_recv_wait': d(34, 35),
-                'll.combine_recv_reduce': d(35, 36), 'll.total': d(24, 36)}
+                'll.combine_recv_reduce': d(35, 36), 'll.total': d(24, 36),
+                # raw %globaltimer stamps (ns), to line up the ranks of one node
+                'abs.dispatch_start': t[0], 'abs.dispatch_end': t[6], 'abs.combine_start': t[16],
+                'abs.combine_end': t[19]}
 
     def barrier(self) -> None:
         """Device-side barrier over the EP group (epoch flags in peer memory, bounded wait)."""

@@ -188,7 +188,7 @@ def test_heap_layout_regions_fit_and_guards_separate_them(R, M, Mll, H, K, E):
     rs = L['row_stride']
     assert rs >= 2 * H and rs % 16 == 0
     ins = L['inbox_stride']
-    assert ins % 16 == 0 and ins >= 2 * H + 8 * K + 4                 # 16-bit dispatch row + metadata
+    assert ins % 128 == 0 and ins >= 2 * H + 8 * K + 4                 # 16-bit dispatch row + metadata
     G = L['max_grid']
     single = {'inbox': R * M * ins, 'nd_nte': E * 4, 'nd_rcnt': G * R * 4, 'info': R * G * 16, 'prog': R * G * 8}
     need = {'ll_rows': R * Mll * rs, 'll_ids': R * Mll * K * 4, 'lc_rows': Mll * K * 2 * H}
