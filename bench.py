@@ -436,6 +436,8 @@ def bench_ll(args, buf, rank, dev, control, graph: bool = True, hook: bool = Tru
             dist.barrier(group=control)
             times[name] = max_over_ranks(_events_us(gg.replay, 20))
             del gg
+            if args.trace and trace is not None:
+                trace.update({f'{name}.{k}': v for k, v in buf.device_trace().items() if k.startswith('ll.')})
         gemm_us = max_over_ranks(_events_us(lambda: a @ b, 20))
         res['hook_overlap'] = {'gemm': '2048x7168 @ 7168x7168 bf16', 'gemm_us': round(gemm_us, 2),
                                'serial_us': round(times['serial'], 2), 'hooked_us': round(times['hooked'], 2),

@@ -49,10 +49,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     auto pair = [](const int64_t (&v)[2]) { return py::make_tuple(v[0], v[1]); };
     d["inbox_stride"] = L.inbox_stride;
     d["inbox"] = L.inbox;
+    d["cinbox_stride"] = L.cinbox_stride;
+    d["cinbox"] = L.cinbox;
     d["nd_nte"] = L.nd_nte;
     d["nd_rcnt"] = L.nd_rcnt;
     d["info"] = L.info;
     d["prog"] = L.prog;
+    d["cprog"] = L.cprog;
     d["max_grid"] = kMaxGrid;
     d["ll_rows"] = pair(L.ll_rows);
     d["ll_ids"] = pair(L.ll_ids);

@@ -2,13 +2,15 @@
 // peer of the EP group through CUDA IPC. All ranks compute the same offsets
 // from the same HeapConfig, so a region of rank p is reached as base[p] + off.
 //
-// Normal mode has one inbox per rank: R blocks of M rows, block s holding the
-// rows source s pushed to this rank (dispatch) or the rows expert rank s sent
-// back (combine). Both ops share it under one op sequence number q: a source
-// writes into a peer's inbox (and its progress / info words) for op q only after
-// that peer reported that it finished reading its inbox for op q - 1, so nothing
-// is double-buffered and nothing is ever reset. Low-latency mode keeps two
-// parities of its own receive areas (its own protocol, no host sync).
+// Normal mode has two inboxes per rank, each R blocks of M rows: block s of the dispatch
+// inbox holds the rows source s pushed to this rank, block s of the combine inbox the rows
+// expert rank s sent back. Each kind of op has its own sequence number: a source writes into
+// a peer's inbox of one kind (and its progress / info words) for op q only after that peer
+// reported that it finished reading that inbox for op q - 1. With separate inboxes a rank's
+// combine does not wait for the peers to finish reading their dispatch rows (and the next
+// dispatch not for the peers' combines), so the ranks are not held in lockstep between ops;
+// nothing is double-buffered and nothing is ever reset. Low-latency mode keeps two parities
+// of its own receive areas (its own protocol, no host sync).
 #pragma once
 
 #include <cstdint>
@@ -34,7 +36,8 @@ enum TracePoint : int {
 };
 
 enum EpochId : int {
-  kEpInbox = 0,   // normal-mode op sequence (dispatch and combine share the inbox)
+  kEpInbox = 0,   // normal-mode dispatch sequence (dispatch inbox)
+  kEpCInbox = 1,  // normal-mode combine sequence (combine inbox)
   kEpLLD = 2,     // low-latency dispatch (send kernel advances it)
   kEpLLC = 3,     // low-latency combine (send kernel advances it)
   kEpBar = 4,     // device barrier
@@ -50,7 +53,8 @@ constexpr int kMaxGrid = 256;
 struct Signals {
   uint64_t nd_cnt[B200EP_MAX_RANKS];    // (q << 32) | rows source s sends this rank
   uint64_t nd_grid[B200EP_MAX_RANKS];   // (q << 32) | CTAs of source s's dispatch kernel
-  uint32_t inbox_free[B200EP_MAX_RANKS];  // peer p finished reading its own inbox for op q
+  uint32_t inbox_free[B200EP_MAX_RANKS];   // peer p finished reading its dispatch inbox for dispatch q
+  uint32_t cinbox_free[B200EP_MAX_RANKS];  // peer p finished reading its combine inbox for combine q
   uint64_t ll_hdr[2][B200EP_MAX_RANKS];     // (epoch << 32) | num_tokens of source s
   uint32_t ll_cnt[2][B200EP_MAX_RANKS];     // cumulative token slots source s has written (per parity)
   uint32_t lc_cnt[2][B200EP_MAX_RANKS];     // cumulative combine rows rank r has written home
@@ -82,12 +86,15 @@ struct HeapConfig {
 struct HeapLayout {
   int64_t sig, local;
   int64_t row_stride;      // bytes per low-latency row: 2H rounded up to 128; fp8 rows use [H payload | H/32 scales]
-  int64_t inbox_stride;    // bytes per inbox row: payload, scales, top-k ids and weights, source token
-  int64_t inbox;           // [R][M] rows of inbox_stride bytes
+  int64_t inbox_stride;    // bytes per dispatch inbox row: payload, scales, top-k ids and weights, source token
+  int64_t inbox;           // dispatch inbox: [R][M] rows of inbox_stride bytes
+  int64_t cinbox_stride;   // bytes per combine inbox row: 16-bit payload, top-k weights
+  int64_t cinbox;          // combine inbox: [R][M] rows of cinbox_stride bytes
   int64_t nd_nte;          // [E] int32: this rank's tokens per expert (read by peers)
   int64_t nd_rcnt;         // [kMaxGrid][R] int32: rows of each CTA's token range per destination
   int64_t info;            // [R][kMaxGrid][2] uint64: (q << 32) | first row, (q << 32) | rows of (source, CTA)
-  int64_t prog;            // [R][kMaxGrid] uint64: (q << 32) | rows (source, CTA) has pushed here
+  int64_t prog;            // [R][kMaxGrid] uint64: (q << 32) | rows dispatch (source, CTA) has pushed here
+  int64_t cprog;           // [R][kMaxGrid] uint64: (q << 32) | rows combine (expert rank, CTA) has pushed here
   // low-latency dispatch receive (x2): [R][Mll] rows, [R][Mll][K] ids
   int64_t ll_rows[2], ll_ids[2];
   // low-latency combine receive (x2): [Mll][K] rows of 2H bytes
@@ -97,12 +104,12 @@ struct HeapLayout {
 
 __host__ __device__ inline int64_t align_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
-// Inbox row: [payload: 2H (16-bit) or H (fp8) | fp8 scales: H/32 | ids: 4K | weights: 4K | token: 4]
-// for dispatch, [payload: 2H | weights: 4K] for combine; the 16-bit dispatch row is the longest.
-// Rows start on 128-byte lines, so a warp's 512-byte run of 16-byte stores covers whole lines
-// (a run that starts mid-line leaves partly written 32-byte sectors at both ends, each one a
-// masked write over NVLink).
+// Dispatch inbox row: [payload: 2H (16-bit) or H (fp8) | fp8 scales: H/32 | ids: 4K | weights: 4K |
+// token: 4]; combine inbox row: [payload: 2H | weights: 4K]. Rows start on 128-byte lines, so a
+// warp's 512-byte run of 16-byte stores covers whole lines (a run that starts mid-line leaves
+// partly written 32-byte sectors at both ends, each one a masked write over NVLink).
 __host__ __device__ inline int64_t inbox_row_bytes(int64_t H, int64_t K) { return align_up(2 * H + 8 * K + 4, 128); }
+__host__ __device__ inline int64_t cinbox_row_bytes(int64_t H, int64_t K) { return align_up(2 * H + 4 * K, 128); }
 
 // Every region is followed by a 256-byte guard zone that the host fills with kCanaryByte at
 // construction and checks on request (SymmHeap::check_canaries): a kernel that writes past
@@ -127,10 +134,13 @@ inline HeapLayout make_layout(const HeapConfig& c, int64_t* guards = nullptr, in
   L.row_stride = align_up(2LL * c.H, 128);
   L.inbox_stride = inbox_row_bytes(c.H, c.K);
   L.inbox = take(int64_t(c.R) * c.M * L.inbox_stride);
+  L.cinbox_stride = cinbox_row_bytes(c.H, c.K);
+  L.cinbox = take(int64_t(c.R) * c.M * L.cinbox_stride);
   L.nd_nte = take(int64_t(c.E) * 4);
   L.nd_rcnt = take(int64_t(kMaxGrid) * c.R * 4);
   L.info = take(int64_t(c.R) * kMaxGrid * 16);
   L.prog = take(int64_t(c.R) * kMaxGrid * 8);
+  L.cprog = take(int64_t(c.R) * kMaxGrid * 8);
   for (int b = 0; b < 2; ++b) {
     L.ll_rows[b] = take(int64_t(c.R) * c.Mll * L.row_stride);
     L.ll_ids[b] = take(int64_t(c.R) * c.Mll * c.K * 4);

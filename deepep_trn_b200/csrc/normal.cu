@@ -28,10 +28,11 @@
 //
 // Ordering: payload stores, a block barrier, then a system-scope fence and release store
 // of the progress word by one thread per destination; receivers poll the word with
-// GPU-scope loads and acquire it at system scope before reading rows. A rank writes into a peer's inbox (and progress / info
-// words) for op q only after that peer reported that it finished reading its inbox for
-// op q - 1 (inbox_free), which every rank sends at the end of its kernel. Every wait is
-// bounded by the buffer's timeout and reports into the host-mapped status page.
+// system-scope relaxed loads and acquire it before reading rows. Dispatch and combine have
+// separate inboxes, progress words and sequence numbers: a rank writes into a peer's inbox
+// of one kind for op q only after that peer reported that it finished reading that inbox
+// for op q - 1 (inbox_free / cinbox_free), which every rank sends at the end of its kernel.
+// Every wait is bounded by the buffer's timeout and reports into the host-mapped status page.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -153,30 +154,36 @@ __device__ bool grid_barrier(LocalState* ls, const HeapView& hv, uint32_t op) {
   return s_ok != 0;
 }
 
-// Last CTA to arrive ends the op: publishes the sequence number locally and tells every
-// peer that this rank's inbox may be written for the next op.
-__device__ void finish_op(LocalState* ls, const HeapView& hv, uint32_t q, int trace_point) {
+// Last CTA to arrive ends the op: publishes the sequence number of its kind (kEpInbox for
+// dispatch, kEpCInbox for combine) locally and tells every peer that this rank's inbox of that
+// kind may be written for the next op.
+__device__ void finish_op(LocalState* ls, const HeapView& hv, int which, uint32_t q, int trace_point) {
   __shared__ int s_last;
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    s_last = atomicAdd(&ls->arrive[kEpInbox], 1u) == gridDim.x - 1;
+    s_last = atomicAdd(&ls->arrive[which], 1u) == gridDim.x - 1;
   }
   __syncthreads();
   if (!s_last) return;
   if (threadIdx.x == 0) {
-    ls->arrive[kEpInbox] = 0;
-    ls->epoch[kEpInbox] = q;
+    ls->arrive[which] = 0;
+    ls->epoch[which] = q;
     ls->trace[trace_point] = global_ns();
   }
-  if (threadIdx.x < hv.R) st_release_sys(&hv.sig(threadIdx.x)->inbox_free[hv.rank], q);
+  if (threadIdx.x < hv.R) {
+    Signals* sp = hv.sig(threadIdx.x);
+    st_release_sys(which == kEpInbox ? &sp->inbox_free[hv.rank] : &sp->cinbox_free[hv.rank], q);
+  }
 }
 
-// Wait (threads < R) until every peer finished reading its inbox for op q - 1.
-__device__ void wait_inboxes_free(const HeapView& hv, uint32_t q, int* s_fail) {
+// Wait (threads < R) until every peer finished reading its inbox of kind `which` for op q - 1.
+__device__ void wait_inboxes_free(const HeapView& hv, int which, uint32_t q, int* s_fail) {
   if (threadIdx.x < hv.R && threadIdx.x != hv.rank) {
-    if (!wait_epoch(&hv.sig(hv.rank)->inbox_free[threadIdx.x], q - 1u, hv.timeout_ns, hv.status, kTimeoutReady, 10,
-                    hv.rank, threadIdx.x))
+    Signals* sp = hv.sig(hv.rank);
+    const uint32_t* f = which == kEpInbox ? &sp->inbox_free[threadIdx.x] : &sp->cinbox_free[threadIdx.x];
+    if (!wait_epoch(f, q - 1u, hv.timeout_ns, hv.status, kTimeoutReady, which == kEpInbox ? 10 : 11, hv.rank,
+                    threadIdx.x))
       atomicExch(s_fail, 1);
   }
 }
@@ -362,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
     ls->trace[kTrNdWaitNs] = 0;
   }
   __syncthreads();
-  wait_inboxes_free(hv, q, &s_fail);
+  wait_inboxes_free(hv, kEpInbox, q, &s_fail);
 
   // ---------------------------------------------------------------- scan
   for (int tt = t0; tt < t1; tt += kThreads) {
@@ -632,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
   }
   if (b == 0 && tid == 0) ls->trace[kTrNdRecvd] = global_ns();
   __syncthreads();
-  finish_op(ls, hv, q, kTrNdEnd);
+  finish_op(ls, hv, kEpInbox, q, kTrNdEnd);
 }
 
 void nd_dispatch(SymmHeap& heap, const at::Tensor& x, const OptTensor& x_scales, int64_t mode, bool round_scale,
@@ -797,11 +804,11 @@ template <typename T16>
 __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
   const HeapView& hv = a.hv;
   LocalState* ls = hv.local();
-  const uint32_t q = ldv_u32(&ls->epoch[kEpInbox]) + 1u;
+  const uint32_t q = ldv_u32(&ls->epoch[kEpCInbox]) + 1u;
   const int me = hv.rank, R = hv.R, M = hv.cfg.M, H = a.H, K = a.K;
   const int G = gridDim.x, b = blockIdx.x;
   const int tid = threadIdx.x, lane = lane_id(), warp = warp_id();
-  const int64_t IS = hv.L.inbox_stride;
+  const int64_t IS = hv.L.cinbox_stride;
   const int64_t RB = 2LL * H;
 
   __shared__ int s_fail;
@@ -819,7 +826,7 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
     ls->trace[kTrNcWaitNs] = 0;
   }
   __syncthreads();
-  wait_inboxes_free(hv, q, &s_fail);
+  wait_inboxes_free(hv, kEpCInbox, q, &s_fail);
   __syncthreads();
   const bool fail0 = s_fail != 0;
 
@@ -841,7 +848,7 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
       if (s < 0) break;
       const int64_t j = s_start[s] + u;
       const int64_t i = s_off[s] + j;
-      uint8_t* dst = hv.base[s] + hv.L.inbox + (static_cast<int64_t>(me) * M + j) * IS;
+      uint8_t* dst = hv.base[s] + hv.L.cinbox + (static_cast<int64_t>(me) * M + j) * IS;
       if (a.pairs)
         push_pair_row<T16>(a, i, dst);
       else
@@ -854,7 +861,7 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
   // one release per source covers every row of its range (an empty range too)
   if (!fail0 && tid < R && (tid != me || a.pairs)) {
     fence_sys();
-    st_release_sys64(hv.at<uint64_t>(tid, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
+    st_release_sys64(hv.at<uint64_t>(tid, hv.L.cprog) + static_cast<int64_t>(me) * kMaxGrid + b,
                      (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(s_cnt[tid]));
   }
   if (b == 0 && tid == 0) ls->trace[kTrNcPublished] = global_ns();
@@ -869,7 +876,7 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
   uint64_t waited = 0;
   if (!fail0 && tid < R && (tid != me || a.pairs)) {
     const uint64_t tw = global_ns();
-    if (wait_tagged(hv.at<uint64_t>(me, hv.L.prog) + static_cast<int64_t>(tid) * kMaxGrid + b, q, hv,
+    if (wait_tagged(hv.at<uint64_t>(me, hv.L.cprog) + static_cast<int64_t>(tid) * kMaxGrid + b, q, hv,
                     kTimeoutCombine, 3, tid) < 0)
       s_wfail = 1;
     waited = global_ns() - tw;
@@ -884,7 +891,7 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
     const int t1 = static_cast<int>(static_cast<int64_t>(a.T) * (b + 1) / G);
     __shared__ const uint8_t* s_rows[kWarps][B200EP_MAX_RANKS];
     __shared__ const float* s_wrows[kWarps][B200EP_MAX_RANKS];
-    const uint8_t* inbox = hv.at<uint8_t>(me, hv.L.inbox);
+    const uint8_t* inbox = hv.at<uint8_t>(me, hv.L.cinbox);
     const int nch = H / 8;
     const bool wfail = s_wfail != 0;
     for (int t = t0 + rw; t < t1 && !wfail; t += kWarps) {
@@ -976,7 +983,7 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
   }
   __syncthreads();
   if (b == 0 && tid == 0) ls->trace[kTrNcReduced] = global_ns();
-  finish_op(ls, hv, q, kTrNcEnd);
+  finish_op(ls, hv, kEpCInbox, q, kTrNcEnd);
 }
 
 void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const at::Tensor& recv_off,
