@@ -26,12 +26,18 @@ enum TracePoint : int {
   // word released
   kTrNdStart = 0, kTrNdScanned, kTrNdCounts, kTrNdNotified, kTrNdPushed, kTrNdRecvd, kTrNdEnd, kTrNdPublished,
   kTrNdWaitNs = 8,  // not a stamp: mean ns a receiving warp of CTA 0 waited for progress words
+  kTrNdFreeIn = 9,  // CTA 0: every peer's dispatch inbox is free (the scan follows)
+  kTrNdBarrier,     // CTA 0: past the grid barrier of the scan
   // normal combine: kernel start, CTA 0's pushes done, CTA 0's reduction done, kernel end,
   // CTA 0's last progress word released
   kTrNcStart = 16, kTrNcPushed, kTrNcReduced, kTrNcEnd, kTrNcPublished,
   kTrNcWaitNs = 21,  // not a stamp: mean ns a reducing warp of CTA 0 waited for progress words
-  kTrLLSendStart = 24, kTrLLSendEnd, kTrLLRecvStart, kTrLLRecvReady, kTrLLRecvEnd,
-  kTrLCSendStart = 32, kTrLCSendEnd, kTrLCRecvStart, kTrLCRecvReady, kTrLCRecvEnd,
+  // low-latency send kernels also stamp when CTA 0 has issued its row stores and when its
+  // releases (the fence that waits for those stores to land) are done
+  kTrLLSendStart = 24, kTrLLSendEnd, kTrLLRecvStart, kTrLLRecvReady, kTrLLRecvEnd, kTrLLSendStored,
+  kTrLLSendReleased,
+  kTrLCSendStart = 32, kTrLCSendEnd, kTrLCRecvStart, kTrLCRecvReady, kTrLCRecvEnd, kTrLCSendStored,
+  kTrLCSendReleased,
   kTracePoints = 40,
 };
 
@@ -90,7 +96,7 @@ struct HeapLayout {
   int64_t inbox;           // dispatch inbox: [R][M] rows of inbox_stride bytes
   int64_t cinbox_stride;   // bytes per combine inbox row: 16-bit payload, top-k weights
   int64_t cinbox;          // combine inbox: [R][M] rows of cinbox_stride bytes
-  int64_t nd_nte;          // [E] int32: this rank's tokens per expert (read by peers)
+  int64_t nd_nte;          // [R][E/R] int32: tokens each source sends to each local expert (written by the sources)
   int64_t nd_rcnt;         // [kMaxGrid][R] int32: rows of each CTA's token range per destination
   int64_t info;            // [R][kMaxGrid][2] uint64: (q << 32) | first row, (q << 32) | rows of (source, CTA)
   int64_t prog;            // [R][kMaxGrid] uint64: (q << 32) | rows dispatch (source, CTA) has pushed here

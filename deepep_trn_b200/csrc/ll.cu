@@ -158,10 +158,12 @@ __global__ void __launch_bounds__(kLLThreads) ll_dispatch_send_kernel(LLSendArgs
     }
     __syncthreads();
   }
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLLSendStored] = global_ns();
   if (tid < R && t1 > t0) {
     fence_sys();
     red_add_release_sys(&hv.sig(tid)->ll_cnt[slot][me], static_cast<uint32_t>(t1 - t0));
   }
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLLSendReleased] = global_ns();
   finish_epoch(ls, kEpLLD, e, kTrLLSendEnd);
 }
 
@@ -498,10 +500,12 @@ __global__ void __launch_bounds__(kLLThreads) ll_combine_send_kernel(LCSendArgs 
     if (lane == 0) atomicAdd(&s_n[s], 1u);
   }
   __syncthreads();
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLCSendStored] = global_ns();
   if (tid < R && s_n[tid] > 0) {
     fence_sys();
     red_add_release_sys(&hv.sig(tid)->lc_cnt[slot][hv.rank], s_n[tid]);
   }
+  if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLCSendReleased] = global_ns();
   finish_epoch(ls, kEpLLC, e, kTrLCSendEnd);
 }
 

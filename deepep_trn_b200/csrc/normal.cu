@@ -370,6 +370,10 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
   }
   __syncthreads();
   wait_inboxes_free(hv, kEpInbox, q, &s_fail);
+  if (b == 0) {  // block-uniform
+    __syncthreads();
+    if (tid == 0) ls->trace[kTrNdFreeIn] = global_ns();
+  }
 
   // ---------------------------------------------------------------- scan
   for (int tt = t0; tt < t1; tt += kThreads) {
@@ -384,6 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
   int32_t* rcnt = hv.at<int32_t>(me, hv.L.nd_rcnt);
   if (tid < R) rcnt[b * R + tid] = s_cnt[tid];
   if (!grid_barrier(ls, hv, 1) && tid == 0) s_fail = 1;
+  if (b == 0 && tid == 0) ls->trace[kTrNdBarrier] = global_ns();
   for (int r = warp; r < R; r += kWarps) {
     int before = 0, all = 0;
     for (int c = lane; c < G; c += 32) {
@@ -448,7 +453,13 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
     }
     if (b == 0) {
       if (a.nte)
-        for (int i = tid; i < a.E; i += kThreads) hv.at<int32_t>(me, hv.L.nd_nte)[i] = a.nte[i];
+        for (int i = tid; i < a.E; i += kThreads) {
+          // destination p gets this rank's counts of p's experts in its own memory, so the
+          // receiver sums them locally (a remote read's reply would queue behind the row
+          // pushes arriving over the same link)
+          const int EL = a.E / R, p = i / EL;
+          hv.at<int32_t>(p, hv.L.nd_nte)[me * EL + (i - p * EL)] = a.nte[i];
+        }
       __syncthreads();
       if (tid < R) {
         fence_sys();
@@ -525,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
     for (int le = tid; le < EL && le < 1024; le += kThreads) {
       int32_t sum = 0;
       if (!rfail && a.nte)
-        for (int s = 0; s < R; ++s) sum += ldv_i32(hv.at<int32_t>(s, hv.L.nd_nte) + me * EL + le);
+        for (int s = 0; s < R; ++s) sum += ldv_i32(hv.at<int32_t>(me, hv.L.nd_nte) + s * EL + le);
       host->notify.per_expert[le] = sum;
     }
     if (tid == 0) {

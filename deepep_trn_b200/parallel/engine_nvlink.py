@@ -105,7 +105,7 @@ class NvlinkEngine:
 
         def d(a, b):
             return round((t[b] - t[a]) / 1e3, 2) if t[a] and t[b] else None
-        return {'dispatch.scan': d(0, 1), 'dispatch.counts_in': d(0, 2), 'dispatch.notified': d(0, 3),
+        return {'dispatch.inbox_free': d(0, 9), 'dispatch.grid_barrier': d(0, 10), 'dispatch.scan': d(0, 1), 'dispatch.counts_in': d(0, 2), 'dispatch.notified': d(0, 3),
                 'dispatch.cta0_pushed': d(0, 4), 'dispatch.cta0_received': d(0, 5), 'dispatch.total': d(0, 6),
                 'dispatch.cta0_published': d(0, 7), 'combine.cta0_published': d(16, 20),
                 'dispatch.cta0_recv_wait': round(t[8] / 1e3, 2), 'combine.cta0_reduce_wait': round(t[21] / 1e3, 2),
@@ -116,6 +116,8 @@ class NvlinkEngine:
                 'll.dispatch_recv_copy': d(27, 28), 'll.gap_to_combine': d(28, 32), 'll.combine_send': d(32, 33),
                 'll.gap_send_to_recv2': d(33, 34), 'll.combine_recv_wait': d(34, 35),
                 'll.combine_recv_reduce': d(35, 36), 'll.total': d(24, 36),
+                'll.send_cta0_stored': d(24, 29), 'll.send_cta0_released': d(24, 30),
+                'll.combine_send_cta0_stored': d(32, 37), 'll.combine_send_cta0_released': d(32, 38),
                 # raw %globaltimer stamps (ns), to line up the ranks of one node
                 'abs.dispatch_start': t[0], 'abs.dispatch_end': t[6], 'abs.combine_start': t[16],
                 'abs.combine_end': t[19]}
