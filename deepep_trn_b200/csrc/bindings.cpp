@@ -68,6 +68,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     return d;
   });
   m.def("layout", &layout);
+  m.def("layout_op", &layout_op);
+  m.def("dispatch_op", &dispatch_op);
+  m.def("combine_op", &combine_op);
   m.def("nd_dispatch", &nd_dispatch);
   m.def("nc_combine", &nc_combine);
   m.def("ll_dispatch_send", &ll_dispatch_send);

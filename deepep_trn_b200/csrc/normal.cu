@@ -469,9 +469,16 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
       if (tid == 0) ls->trace[kTrNdScanned] = global_ns();
     }
   }
+  // Every CTA's control words (its range's first row and rows, CTA 0's totals and per-expert
+  // counts) leave before any CTA pushes rows: queued behind the other CTAs' row traffic, CTA
+  // 0's totals landed ~70 us late at EP2, and a receiver cannot place any row before it has
+  // every source's total. The barrier is taken on every path (errors included).
+  if (!grid_barrier(ls, hv, 2) && tid == 0) s_fail = 1;
+  __syncthreads();
+  const bool fail1 = s_fail != 0;
 
   // ---------------------------------------------------------------- push (every warp)
-  if (!fail0) {
+  if (!fail1) {
     for (int t = t0 + warp; t < t1; t += kWarps) {
       uint32_t m = 0;
       if (lane < R) {
@@ -488,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
   __syncthreads();
   if (b == 0 && tid == 0) ls->trace[kTrNdPushed] = global_ns();
   // one release per destination covers every row of this CTA's range (an empty range too)
-  if (!fail0 && tid < R && tid != me) {
+  if (!fail1 && tid < R && tid != me) {
     fence_sys();
     st_release_sys64(hv.at<uint64_t>(tid, hv.L.prog) + static_cast<int64_t>(me) * kMaxGrid + b,
                      (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(s_cnt[tid]));
@@ -497,9 +504,9 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
 
   // ---------------------------------------------------------------- receive (every warp)
   __shared__ int s_rfail;
-  if (tid == 0) s_rfail = fail0 ? 1 : 0;
+  if (tid == 0) s_rfail = fail1 ? 1 : 0;
   __syncthreads();
-  if (tid < R && !fail0) {
+  if (tid < R && !fail1) {
     const int64_t c = wait_tagged(&hv.sig(me)->nd_cnt[tid], q, hv, kTimeoutReady, 1, tid);
     const int64_t g = c < 0 ? -1 : wait_tagged(&hv.sig(me)->nd_grid[tid], q, hv, kTimeoutReady, 1, tid);
     if (c < 0 || g < 0) {

@@ -5,6 +5,7 @@
 #include <chrono>
 #include <cstdint>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include <ATen/ATen.h>
@@ -78,6 +79,21 @@ void nc_combine(SymmHeap& heap, const at::Tensor& x, const OptTensor& w, const a
                 const at::Tensor& recv_info, const at::Tensor& token_pos, const at::Tensor& send_start, at::Tensor out,
                 const OptTensor& out_w, const OptTensor& bias0, const OptTensor& bias1, int64_t grid,
                 const OptTensor& pair_pos, const OptTensor& pair_w);
+
+// host_ops.cpp: the normal-mode ops as one native call each (outputs, launch, notify wait)
+std::tuple<at::Tensor, at::Tensor, at::Tensor> layout_op(const at::Tensor& topk_idx, int64_t num_experts,
+                                                         int64_t num_ranks, at::Tensor scratch);
+std::tuple<at::Tensor, OptTensor, OptTensor, OptTensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor, at::Tensor,
+           int64_t, std::vector<int64_t>>
+dispatch_op(SymmHeap& heap, const at::Tensor& x, const OptTensor& x_scales, int64_t mode, bool round_scale,
+            const OptTensor& topk_idx, const OptTensor& topk_w, const OptTensor& nte, const at::Tensor& in_rank,
+            int64_t num_experts, int64_t grid, int64_t cap, bool pad_rows, bool wait, int64_t ticket,
+            double timeout_s);
+std::tuple<at::Tensor, OptTensor> combine_op(SymmHeap& heap, const at::Tensor& x, const OptTensor& w,
+                                             const at::Tensor& recv_off, const at::Tensor& recv_info,
+                                             const at::Tensor& token_pos, const at::Tensor& send_start,
+                                             const OptTensor& bias0, const OptTensor& bias1, int64_t grid,
+                                             const OptTensor& pair_pos, const OptTensor& pair_w);
 
 // ll.cu
 void ll_dispatch_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& topk_idx, int64_t num_experts,

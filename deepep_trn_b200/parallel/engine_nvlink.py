@@ -172,11 +172,8 @@ class NvlinkEngine:
         need = self.R + num_experts + 1
         if self._scratch is None or self._scratch.numel() < need or self._scratch.device != dev:
             self._scratch = torch.zeros(need, dtype=torch.int32, device=dev)
-        ntr = torch.empty(self.R, dtype=torch.int32, device=dev)
-        nte = torch.empty(num_experts, dtype=torch.int32, device=dev)
-        itr = torch.empty(T, self.R, dtype=torch.bool, device=dev)
         with timer.stage('layout'):
-            self.C.layout(topk_idx.contiguous(), num_experts, self.R, ntr, nte, itr, self._scratch)
+            ntr, nte, itr = self.C.layout_op(topk_idx, num_experts, self.R, self._scratch)
         return ntr, nte, itr
 
     # ------------------------------------------------------------------ normal mode
@@ -205,65 +202,43 @@ class NvlinkEngine:
         mode = 1 if fp8_in else (2 if use_fp8 else 0)
         R = self.R
         G = self._grid(config)
-        token_pos = torch.empty(T, R, dtype=torch.int32, device=dev)
-        send_start = torch.empty(G, R, dtype=torch.int32, device=dev)
-        recv_info = torch.empty(R, self.max_grid, 2, dtype=torch.int32, device=dev)
-        recv_off = torch.empty(R + 1, dtype=torch.int64, device=dev)
         self.ticket += 1
         x_scales = x[1].float() if fp8_in else None
         # Outputs are sized for the worst case (every peer sends its full capacity) so the kernel
         # is queued before the host learns the receive size; the host then waits on the notify
-        # ticket while the GPU is still moving rows, and returns the first N rows.
+        # ticket while the GPU is still moving rows, and gets the first N rows.
         if num_worst_tokens:
             cap = int(num_worst_tokens)
         elif cached:
             cap = handle.num_recv if handle.num_recv is not None else handle.capacity
         else:
             cap = R * self.M
-        if mode == 0:
-            recv_x = torch.empty(cap, H, dtype=xt.dtype, device=dev)
-            recv_s = None
-        else:
-            recv_x = torch.empty(cap, H, dtype=torch.float8_e4m3fn, device=dev)
-            recv_s = torch.empty(cap, H // 128, dtype=torch.float32, device=dev)
-        recv_topk = recv_w = None
-        if not cached:
-            recv_topk = torch.empty(cap, K, dtype=topk_idx.dtype, device=dev)
-            if topk_weights is not None:
-                recv_w = torch.empty(cap, K, dtype=torch.float32, device=dev)
-        recv_src = torch.empty(cap, dtype=torch.int64, device=dev)
-        with timer.stage('dispatch'):
-            self.C.nd_dispatch(self.heap, xt if not fp8_in else xt.view(torch.uint8), x_scales, mode,
-                               bool(round_scale),
-                               None if cached else _contig(topk_idx),
-                               None if (cached or topk_weights is None) else _contig(_f32(topk_weights)),
-                               None if cached else _contig(nte if nte.dtype == torch.int32 else nte.to(torch.int32)),
-                               _contig(itr), token_pos, send_start, recv_info, recv_off,
-                               recv_x, recv_s, recv_topk, recv_w, recv_src, E, self.ticket, G,
-                               bool(num_worst_tokens))
+        wait = not (num_worst_tokens or cached)
+        try:
+            with timer.stage('dispatch'):
+                (recv_x, recv_s, recv_topk, recv_w, recv_src, token_pos, send_start, recv_info, recv_off, N,
+                 notify) = self.C.dispatch_op(
+                    self.heap, xt, x_scales, mode, bool(round_scale),
+                    None if cached else _contig(topk_idx),
+                    None if (cached or topk_weights is None) else _contig(_f32(topk_weights)),
+                    None if cached else _contig(nte if nte.dtype == torch.int32 else nte.to(torch.int32)),
+                    _contig(itr), E, G, cap, bool(num_worst_tokens), wait, self.ticket, self.host_timeout_s)
+        except RuntimeError:
+            if not wait:
+                raise
+            # every wait of the queued kernel is bounded: let it finish so nothing of this op
+            # is in flight, then raise with the device's own record
+            torch.cuda.synchronize()
+            self.check()
+            raise
         per_expert = recv_counts = None
-        if num_worst_tokens or cached:
-            N = cap
+        if not wait:
             recv_counts = handle.recv_counts if cached else None
         else:
-            with timer.stage('notify_wait'):
-                try:
-                    info = self.heap.wait_notify(self.ticket, EL, self.host_timeout_s)
-                except RuntimeError:
-                    # every wait of the queued kernel is bounded: let it finish so nothing of
-                    # this op is in flight, then raise with the device's own record
-                    torch.cuda.synchronize()
-                    self.check()
-                    raise
-            N = int(info[0])
-            recv_counts = torch.tensor(info[1:1 + R], dtype=torch.int64)
-            per_expert = info[1 + R:1 + R + EL]
+            recv_counts = torch.tensor(notify[:R], dtype=torch.int64)
+            per_expert = notify[R:R + EL]
             if expert_alignment > 1:
                 per_expert = [(c + expert_alignment - 1) // expert_alignment * expert_alignment for c in per_expert]
-            recv_x, recv_src = recv_x[:N], recv_src[:N]
-            recv_s = recv_s[:N] if recv_s is not None else None
-            recv_topk = recv_topk[:N]
-            recv_w = recv_w[:N] if recv_w is not None else None
         new = DispatchHandle(T, K, None, recv_counts, recv_src, itr, num_recv=None if num_worst_tokens else N,
                              token_pos=token_pos, recv_off=recv_off, hidden=H, num_experts=E)
         new.capacity = cap
@@ -287,10 +262,6 @@ class NvlinkEngine:
             raise ValueError(f'combine needs bf16/fp16 rows, got {x.dtype}')
         K = topk_weights.shape[1] if topk_weights is not None else handle.topk
         self._ensure(self._spec(H, K, handle.num_experts))
-        T = handle.num_tokens
-        out = torch.empty(T, H, dtype=x.dtype, device=x.device)
-        out_w = torch.empty(T, topk_weights.shape[1], dtype=torch.float32, device=x.device) \
-            if topk_weights is not None else None
         b = [t.contiguous() for t in bias]
         xc = x if (x.stride(1) == 1 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0) else x.contiguous()
         pp = pw = None
@@ -299,10 +270,11 @@ class NvlinkEngine:
             pp = pairs[0] if pairs[0].dtype == torch.int32 else pairs[0].to(torch.int32)
             pp, pw = _contig(pp), _contig(_f32(pairs[1]))
         with timer.stage('combine'):
-            self.C.nc_combine(self.heap, xc,
-                              _contig(_f32(topk_weights)) if topk_weights is not None else None,
-                              handle.recv_off, handle.recv_info, handle.token_pos, handle.send_start, out, out_w,
-                              b[0] if len(b) > 0 else None, b[1] if len(b) > 1 else None, handle.grid, pp, pw)
+            out, out_w = self.C.combine_op(self.heap, xc,
+                                           _contig(_f32(topk_weights)) if topk_weights is not None else None,
+                                           handle.recv_off, handle.recv_info, handle.token_pos, handle.send_start,
+                                           b[0] if len(b) > 0 else None, b[1] if len(b) > 1 else None,
+                                           handle.grid, pp, pw)
         if out_w is not None and topk_weights.dtype != torch.float32:
             out_w = out_w.to(topk_weights.dtype)
         return out, out_w, EventOverlap()

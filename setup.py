@@ -11,7 +11,7 @@ from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = Path(__file__).resolve().parent
 CSRC = ROOT / 'deepep_trn_b200' / 'csrc'
-SOURCES = sorted(str(p.relative_to(ROOT)) for p in CSRC.glob('*.cu')) + [str((CSRC / 'bindings.cpp').relative_to(ROOT))]
+SOURCES = sorted(str(p.relative_to(ROOT)) for p in list(CSRC.glob('*.cu')) + list(CSRC.glob('*.cpp')))
 
 NVCC_FLAGS = [
     '-gencode', 'arch=compute_100a,code=sm_100a',
