@@ -28,6 +28,10 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <mutex>
+#include <utility>
+#include <vector>
+
 #include "ops.h"
 
 namespace b200ep {
@@ -66,11 +70,12 @@ struct LLSendArgs {
 };
 
 // grid: CTAs own contiguous blocks of tokens
+// One sending CTA's share (tokens [T*b/G, T*(b+1)/G)) for epoch e; any multiple of 32 threads.
 template <typename T16>
-__global__ void __launch_bounds__(kLLThreads) ll_dispatch_send_kernel(LLSendArgs a) {
+__device__ void ll_dispatch_send_body(const LLSendArgs& a, uint32_t e) {
   const HeapView& hv = a.hv;
   LocalState* ls = hv.local();
-  const uint32_t e = ldv_u32(&ls->epoch[kEpLLD]) + 1u;
+  const int nthr = blockDim.x;
   const int slot = e & 1u;
   const int me = hv.rank, R = hv.R, Mll = hv.cfg.Mll;
   const int64_t rs = hv.L.row_stride;
@@ -106,11 +111,11 @@ __global__ void __launch_bounds__(kLLThreads) ll_dispatch_send_kernel(LLSendArgs
     const T16* src = reinterpret_cast<const T16*>(a.x + static_cast<int64_t>(t) * a.x_stride);
     const int nchunk = H / 8;  // 16-byte chunks of the 16-bit row
     if (!a.use_fp8) {
-      for (int j0 = tid; j0 < nchunk; j0 += 4 * kLLThreads) {
+      for (int j0 = tid; j0 < nchunk; j0 += 4 * nthr) {
         int4 v[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int j = j0 + u * kLLThreads;
+          const int j = j0 + u * nthr;
           if (j < nchunk) v[u] = reinterpret_cast<const int4*>(src)[j];
         }
         for (uint32_t m = dmask; m; m &= m - 1) {
@@ -118,7 +123,7 @@ __global__ void __launch_bounds__(kLLThreads) ll_dispatch_send_kernel(LLSendArgs
           int4* dst = reinterpret_cast<int4*>(hv.base[p] + hv.L.ll_rows[slot] + slot_row * rs);
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const int j = j0 + u * kLLThreads;
+            const int j = j0 + u * nthr;
             if (j < nchunk) dst[j] = v[u];
           }
         }
@@ -126,18 +131,18 @@ __global__ void __launch_bounds__(kLLThreads) ll_dispatch_send_kernel(LLSendArgs
     } else {
       // a half-warp quantises one 128-element block; every thread runs the same number of
       // iterations so the shuffles inside quant8_e4m3 always see full warps
-      const int iters = (nchunk + kLLThreads - 1) / kLLThreads;
+      const int iters = (nchunk + nthr - 1) / nthr;
       for (int it0 = 0; it0 < iters; it0 += 4) {
         float vv[4][8];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int j = (it0 + u) * kLLThreads + tid;
+          const int j = (it0 + u) * nthr + tid;
           load8(vv[u], src + static_cast<int64_t>(j) * 8, it0 + u < iters && j < nchunk);
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
         if (it0 + u >= iters) break;
-        const int j = (it0 + u) * kLLThreads + tid;
+        const int j = (it0 + u) * nthr + tid;
         const bool act = j < nchunk;
         const Quant8 qr = quant8_e4m3(vv[u], a.round_scale);
         if (act) {
@@ -152,7 +157,7 @@ __global__ void __launch_bounds__(kLLThreads) ll_dispatch_send_kernel(LLSendArgs
       }
     }
     // ids go to every rank (a non-routed rank learns that it is not a destination)
-    for (int i = tid; i < R * K; i += kLLThreads) {
+    for (int i = tid; i < R * K; i += nthr) {
       const int p = i / K, k = i % K;
       hv.at<int32_t>(p, hv.L.ll_ids[slot])[slot_row * K + k] = s_ids[k];
     }
@@ -164,12 +169,18 @@ __global__ void __launch_bounds__(kLLThreads) ll_dispatch_send_kernel(LLSendArgs
     red_add_release_sys(&hv.sig(tid)->ll_cnt[slot][me], static_cast<uint32_t>(t1 - t0));
   }
   if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLLSendReleased] = global_ns();
+}
+
+template <typename T16>
+__global__ void __launch_bounds__(kLLThreads) ll_dispatch_send_kernel(LLSendArgs a) {
+  LocalState* ls = a.hv.local();
+  const uint32_t e = ldv_u32(&ls->epoch[kEpLLD]) + 1u;
+  ll_dispatch_send_body<T16>(a, e);
   finish_epoch(ls, kEpLLD, e, kTrLLSendEnd);
 }
 
-void ll_dispatch_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& topk_idx, int64_t num_experts,
-                      bool use_fp8, bool round_scale, int64_t num_sms) {
-  const c10::cuda::CUDAGuard guard(x.device());
+static LLSendArgs ll_send_args(SymmHeap& heap, const at::Tensor& x, const at::Tensor& topk_idx,
+                               int64_t num_experts, bool use_fp8, bool round_scale) {
   HeapView hv = heap.view();
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.element_size() == 2, "x must be 16-bit [T, H]");
   TORCH_CHECK(topk_idx.is_contiguous() && topk_idx.dim() == 2, "topk_idx must be contiguous [T, K]");
@@ -190,8 +201,15 @@ void ll_dispatch_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& top
   TORCH_CHECK(a.K <= 32 && a.K <= hv.cfg.K && a.E <= hv.cfg.E && a.E % hv.R == 0, "bad top-k / experts");
   TORCH_CHECK(a.T == 0 || ((a.x_stride % 16) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0),
               "x rows must be 16-byte aligned");
+  return a;
+}
+
+void ll_dispatch_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& topk_idx, int64_t num_experts,
+                      bool use_fp8, bool round_scale, int64_t num_sms) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  const LLSendArgs a = ll_send_args(heap, x, topk_idx, num_experts, use_fp8, round_scale);
   const int sms = num_sms > 0 ? static_cast<int>(num_sms) : heap.num_sms();
-  const int grid = std::max(1, std::min(std::min(a.T, hv.cfg.Mll), 2 * sms));
+  const int grid = std::max(1, std::min(std::min(a.T, a.hv.cfg.Mll), 2 * sms));
   auto stream = at::cuda::getCurrentCUDAStream();
   if (x.scalar_type() == at::kHalf)
     ll_dispatch_send_kernel<__half><<<grid, kLLThreads, 0, stream>>>(a);
@@ -221,10 +239,10 @@ struct LLRecvArgs {
 // share of the slots: the ids of the earlier slots give it the position of its first row
 // (no communication between the CTAs), and it copies the rows of its own slots. The last
 // CTA of the expert, which has walked every slot, writes the counts and layout_range.
-__global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecvArgs a) {
+// Receive side for epoch e; blockDim.x == kLLRecvThreads, gridDim.x == EL * split.
+__device__ void ll_dispatch_recv_body(const LLRecvArgs& a, uint32_t e) {
   const HeapView& hv = a.hv;
   LocalState* ls = hv.local();
-  const uint32_t e = ldv_u32(&ls->epoch[kEpLLD]);
   const int slot = e & 1u;
   const int me = hv.rank, R = hv.R, Mll = hv.cfg.Mll;
   const int64_t rs = hv.L.row_stride;
@@ -392,10 +410,27 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
   }
 }
 
-void ll_dispatch_recv(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_scales, at::Tensor recv_count,
-                      at::Tensor src_info, at::Tensor layout_range, at::Tensor pair_meta, int64_t num_experts,
-                      bool use_fp8, bool ue8m0, const OptTensor& cum_stats, const OptTensor& wait_stats) {
-  const c10::cuda::CUDAGuard guard(recv_x.device());
+__global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecvArgs a) {
+  ll_dispatch_recv_body(a, ldv_u32(&a.hv.local()->epoch[kEpLLD]));
+}
+
+// Send and receive in one cooperative launch (no receive hook): every CTA sends its tokens,
+// publishes, then receives, so the receive waits overlap the other CTAs' sends and no kernel
+// boundary sits between the halves. All CTAs are resident (cooperative launch), so a CTA
+// waiting for peers never keeps this GPU's own senders off the SMs.
+template <typename T16>
+__global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_fused_kernel(LLSendArgs s, LLRecvArgs r) {
+  LocalState* ls = s.hv.local();
+  const uint32_t e = ldv_u32(&ls->epoch[kEpLLD]) + 1u;
+  ll_dispatch_send_body<T16>(s, e);
+  finish_epoch(ls, kEpLLD, e, kTrLLSendEnd);
+  ll_dispatch_recv_body(r, e);
+}
+
+static LLRecvArgs ll_recv_args(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_scales,
+                               at::Tensor recv_count, at::Tensor src_info, at::Tensor layout_range,
+                               at::Tensor pair_meta, int64_t num_experts, bool use_fp8, bool ue8m0,
+                               const OptTensor& cum_stats, const OptTensor& wait_stats) {
   HeapView hv = heap.view();
   LLRecvArgs a{};
   a.hv = hv;
@@ -419,8 +454,61 @@ void ll_dispatch_recv(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_s
   if (wait_stats.has_value()) a.wait_stats = wait_stats->data_ptr<int64_t>();
   // spread the copies over about 128 CTAs when there are few local experts
   a.split = EL >= 128 ? 1 : std::max(1, std::min(8, 128 / EL));
-  ll_dispatch_recv_kernel<<<EL * a.split, kLLRecvThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  return a;
+}
+
+void ll_dispatch_recv(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_scales, at::Tensor recv_count,
+                      at::Tensor src_info, at::Tensor layout_range, at::Tensor pair_meta, int64_t num_experts,
+                      bool use_fp8, bool ue8m0, const OptTensor& cum_stats, const OptTensor& wait_stats) {
+  const c10::cuda::CUDAGuard guard(recv_x.device());
+  const LLRecvArgs a = ll_recv_args(heap, recv_x, recv_scales, recv_count, src_info, layout_range, pair_meta,
+                                    num_experts, use_fp8, ue8m0, cum_stats, wait_stats);
+  ll_dispatch_recv_kernel<<<(a.E / a.hv.R) * a.split, kLLRecvThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// True if `grid` CTAs of `fn` at `threads` threads are resident at once on this GPU (the
+// occupancy of each kernel is asked once per process).
+static bool fits_resident(const void* fn, int threads, int grid, int num_sms) {
+  static std::mutex mu;
+  static std::vector<std::pair<const void*, int>> known;
+  int per_sm = -1;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& k : known)
+      if (k.first == fn) per_sm = k.second;
+  }
+  if (per_sm < 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0) != cudaSuccess) {
+      (void)cudaGetLastError();
+      per_sm = 0;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    known.emplace_back(fn, per_sm);
+  }
+  return static_cast<int64_t>(per_sm) * num_sms >= grid;
+}
+
+void ll_dispatch(SymmHeap& heap, const at::Tensor& x, const at::Tensor& topk_idx, int64_t num_experts, bool use_fp8,
+                 bool round_scale, at::Tensor recv_x, const OptTensor& recv_scales, at::Tensor recv_count,
+                 at::Tensor src_info, at::Tensor layout_range, at::Tensor pair_meta, bool ue8m0,
+                 const OptTensor& cum_stats, const OptTensor& wait_stats) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  LLSendArgs sa = ll_send_args(heap, x, topk_idx, num_experts, use_fp8, round_scale);
+  LLRecvArgs ra = ll_recv_args(heap, recv_x, recv_scales, recv_count, src_info, layout_range, pair_meta,
+                               num_experts, use_fp8, ue8m0, cum_stats, wait_stats);
+  const int grid = (ra.E / ra.hv.R) * ra.split;
+  void* fn = x.scalar_type() == at::kHalf ? reinterpret_cast<void*>(ll_dispatch_fused_kernel<__half>)
+                                          : reinterpret_cast<void*>(ll_dispatch_fused_kernel<__nv_bfloat16>);
+  if (!fits_resident(fn, kLLRecvThreads, grid, heap.num_sms())) {
+    ll_dispatch_send(heap, x, topk_idx, num_experts, use_fp8, round_scale, 0);
+    ll_dispatch_recv(heap, recv_x, recv_scales, recv_count, src_info, layout_range, pair_meta, num_experts, use_fp8,
+                     ue8m0, cum_stats, wait_stats);
+    return;
+  }
+  void* args[] = {&sa, &ra};
+  AT_CUDA_CHECK(cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kLLRecvThreads), args, 0,
+                                            at::cuda::getCurrentCUDAStream()));
 }
 
 // ============================================================================ combine send
@@ -435,11 +523,11 @@ struct LCSendArgs {
   int H, K, EL;
 };
 
-// persistent grid over (expert, row) items; a CTA copies one row home and flags it
-__global__ void __launch_bounds__(kLLThreads) ll_combine_send_kernel(LCSendArgs a) {
+// persistent grid over (expert, row) items: each warp copies rows home, then the CTA flags
+// what it sent to each rank; blockDim.x == kLLThreads
+__device__ void ll_combine_send_body(const LCSendArgs& a, uint32_t e) {
   const HeapView& hv = a.hv;
   LocalState* ls = hv.local();
-  const uint32_t e = ldv_u32(&ls->epoch[kEpLLC]) + 1u;
   const int slot = e & 1u;
   const int R = hv.R, Mll = hv.cfg.Mll, H = a.H, K = a.K;
   const int64_t RM = static_cast<int64_t>(R) * Mll;
@@ -506,12 +594,17 @@ __global__ void __launch_bounds__(kLLThreads) ll_combine_send_kernel(LCSendArgs 
     red_add_release_sys(&hv.sig(tid)->lc_cnt[slot][hv.rank], s_n[tid]);
   }
   if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLCSendReleased] = global_ns();
+}
+
+__global__ void __launch_bounds__(kLLThreads) ll_combine_send_kernel(LCSendArgs a) {
+  LocalState* ls = a.hv.local();
+  const uint32_t e = ldv_u32(&ls->epoch[kEpLLC]) + 1u;
+  ll_combine_send_body(a, e);
   finish_epoch(ls, kEpLLC, e, kTrLCSendEnd);
 }
 
-void ll_combine_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& recv_count, const at::Tensor& src_info,
-                     const at::Tensor& pair_meta, int64_t num_experts, int64_t num_sms) {
-  const c10::cuda::CUDAGuard guard(x.device());
+static LCSendArgs lc_send_args(SymmHeap& heap, const at::Tensor& x, const at::Tensor& recv_count,
+                               const at::Tensor& src_info, const at::Tensor& pair_meta, int64_t num_experts) {
   HeapView hv = heap.view();
   TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1 && x.element_size() == 2, "x must be 16-bit [EL, rows, H]");
   LCSendArgs a{};
@@ -528,6 +621,13 @@ void ll_combine_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& recv
   TORCH_CHECK(x.size(0) == a.EL && a.EL <= 1024, "x must have one slab per local expert (at most 1024)");
   TORCH_CHECK(a.H % 8 == 0 && a.x_row_stride % 16 == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0,
               "x rows must be 16-byte aligned");
+  return a;
+}
+
+void ll_combine_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& recv_count, const at::Tensor& src_info,
+                     const at::Tensor& pair_meta, int64_t num_experts, int64_t num_sms) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  const LCSendArgs a = lc_send_args(heap, x, recv_count, src_info, pair_meta, num_experts);
   const int sms = num_sms > 0 ? static_cast<int>(num_sms) : heap.num_sms();
   ll_combine_send_kernel<<<sms, kLLThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -543,12 +643,12 @@ struct LCRecvArgs {
   int T, H, K, E;
 };
 
-// grid: one CTA per token; every thread issues the K slot loads of a 16-byte chunk together
+// tokens t = blockIdx.x, blockIdx.x + gridDim.x, ...; every thread issues the K slot loads of
+// a 16-byte chunk together; blockDim.x == kLLThreads
 template <typename T16>
-__global__ void __launch_bounds__(kLLThreads) ll_combine_recv_kernel(LCRecvArgs a) {
+__device__ void ll_combine_recv_body(const LCRecvArgs& a, uint32_t e) {
   const HeapView& hv = a.hv;
   LocalState* ls = hv.local();
-  const uint32_t e = ldv_u32(&ls->epoch[kEpLLC]);
   const int slot = e & 1u;
   const int me = hv.rank, H = a.H, K = a.K;
   const int64_t RB = 2LL * H;
@@ -644,9 +744,23 @@ __global__ void __launch_bounds__(kLLThreads) ll_combine_recv_kernel(LCRecvArgs 
   }
 }
 
-void ll_combine_recv(SymmHeap& heap, const at::Tensor& topk_idx, const at::Tensor& topk_w, at::Tensor out,
-                     int64_t num_sms) {
-  const c10::cuda::CUDAGuard guard(out.device());
+template <typename T16>
+__global__ void __launch_bounds__(kLLThreads) ll_combine_recv_kernel(LCRecvArgs a) {
+  ll_combine_recv_body<T16>(a, ldv_u32(&a.hv.local()->epoch[kEpLLC]));
+}
+
+// Send and receive of a combine in one cooperative launch (no receive hook).
+template <typename T16>
+__global__ void __launch_bounds__(kLLThreads) ll_combine_fused_kernel(LCSendArgs s, LCRecvArgs r) {
+  LocalState* ls = s.hv.local();
+  const uint32_t e = ldv_u32(&ls->epoch[kEpLLC]) + 1u;
+  ll_combine_send_body(s, e);
+  finish_epoch(ls, kEpLLC, e, kTrLCSendEnd);
+  ll_combine_recv_body<T16>(r, e);
+}
+
+static LCRecvArgs lc_recv_args(SymmHeap& heap, const at::Tensor& topk_idx, const at::Tensor& topk_w,
+                               at::Tensor out) {
   HeapView hv = heap.view();
   TORCH_CHECK(out.is_contiguous() && out.element_size() == 2, "out must be contiguous 16-bit [T, H]");
   TORCH_CHECK(topk_idx.is_contiguous() && topk_w.is_contiguous() && topk_w.scalar_type() == at::kFloat,
@@ -662,6 +776,13 @@ void ll_combine_recv(SymmHeap& heap, const at::Tensor& topk_idx, const at::Tenso
   a.K = static_cast<int>(topk_idx.size(1));
   a.E = hv.cfg.E;
   TORCH_CHECK(a.H % 8 == 0 && a.T <= hv.cfg.Mll && a.K <= hv.cfg.K && a.K <= 32, "combine shape exceeds the buffer");
+  return a;
+}
+
+void ll_combine_recv(SymmHeap& heap, const at::Tensor& topk_idx, const at::Tensor& topk_w, at::Tensor out,
+                     int64_t num_sms) {
+  const c10::cuda::CUDAGuard guard(out.device());
+  const LCRecvArgs a = lc_recv_args(heap, topk_idx, topk_w, out);
   if (a.T == 0) return;
   auto stream = at::cuda::getCurrentCUDAStream();
   if (out.scalar_type() == at::kHalf)
@@ -670,6 +791,25 @@ void ll_combine_recv(SymmHeap& heap, const at::Tensor& topk_idx, const at::Tenso
     ll_combine_recv_kernel<__nv_bfloat16><<<a.T, kLLThreads, 0, stream>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   (void)num_sms;
+}
+
+void ll_combine(SymmHeap& heap, const at::Tensor& x, const at::Tensor& recv_count, const at::Tensor& src_info,
+                const at::Tensor& pair_meta, int64_t num_experts, const at::Tensor& topk_idx, const at::Tensor& topk_w,
+                at::Tensor out) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  LCSendArgs sa = lc_send_args(heap, x, recv_count, src_info, pair_meta, num_experts);
+  LCRecvArgs ra = lc_recv_args(heap, topk_idx, topk_w, out);
+  const int grid = heap.num_sms();
+  void* fn = out.scalar_type() == at::kHalf ? reinterpret_cast<void*>(ll_combine_fused_kernel<__half>)
+                                            : reinterpret_cast<void*>(ll_combine_fused_kernel<__nv_bfloat16>);
+  if (!fits_resident(fn, kLLThreads, grid, heap.num_sms())) {
+    ll_combine_send(heap, x, recv_count, src_info, pair_meta, num_experts, 0);
+    ll_combine_recv(heap, topk_idx, topk_w, out, 0);
+    return;
+  }
+  void* args[] = {&sa, &ra};
+  AT_CUDA_CHECK(cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kLLThreads), args, 0,
+                                            at::cuda::getCurrentCUDAStream()));
 }
 
 }  // namespace b200ep
