@@ -233,6 +233,7 @@ def main():
     if args.profile:
         profile_steps(lambda: step(x, idx, w), 'normal d+c', rank)
     if args.trace and args.impl == 'ours':
+        buf._engine.barrier()   # a device barrier: its exit stamp lines up the ranks' clocks
         for _ in range(3):
             step(x, idx, w)
         tr = buf.device_trace()
@@ -240,7 +241,8 @@ def main():
         dist.all_gather_object(everyone, (rank, tr), group=control)
         if rank == 0:
             for r, t in everyone:
-                log(f'device trace rank {r}: ' + ' '.join(f'{k}={v}' for k, v in t.items()))
+                log(f'device trace rank {r}: ' + ' '.join(f'{k}={v}' for k, v in t.items() if k != 'abs.raw'))
+            log_aligned(everyone)
 
     # ---- end to end through the public API: pinned H2D of inputs, D2H of the combined result
     e2e = None
@@ -316,6 +318,24 @@ def main():
         buf.destroy()
     dist.barrier(group=control)
     dist.destroy_process_group()
+
+
+def log_aligned(everyone):
+    """The last step's phase stamps of every rank on one time line (us): each rank's clock is
+    shifted so that the device barrier before the traced steps exits at the same moment."""
+    from deepep_trn_b200.utils.benchutil import log
+    names = {0: 'd.start', 9: 'd.free', 10: 'd.grid_bar', 1: 'd.scanned', 4: 'd.cta0_pushed',
+             7: 'd.cta0_published', 2: 'd.counts_in', 3: 'd.notified', 5: 'd.cta0_recvd', 6: 'd.end',
+             16: 'c.start', 17: 'c.cta0_pushed', 20: 'c.cta0_published', 18: 'c.cta0_reduced', 19: 'c.end'}
+    base = None
+    for r, t in everyone:
+        raw = t.get('abs.raw') or []
+        if len(raw) < 21 or not raw[15]:
+            return
+        rel = {n: (raw[i] - raw[15]) / 1e3 for i, n in names.items() if raw[i]}
+        if base is None:
+            base = rel['d.start']
+        log(f'aligned rank {r}: ' + ' '.join(f'{n}={v - base:.1f}' for n, v in sorted(rel.items(), key=lambda kv: kv[1])))
 
 
 def profile_steps(fn, label, rank, n=3):

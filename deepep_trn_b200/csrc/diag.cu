@@ -20,7 +20,10 @@ __global__ void device_barrier_kernel(HeapView hv) {
     wait_epoch(&hv.sig(hv.rank)->barrier[tid], e, hv.timeout_ns, hv.status, kTimeoutBarrier, 7, hv.rank, tid);
   }
   __syncthreads();
-  if (tid == 0) ls->epoch[kEpBar] = e;
+  if (tid == 0) {
+    ls->epoch[kEpBar] = e;
+    ls->trace[kTrBarrierExit] = global_ns();
+  }
 }
 
 __global__ void wait_probe_kernel(HeapView hv, uint64_t budget_ns) {

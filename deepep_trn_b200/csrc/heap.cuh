@@ -28,6 +28,8 @@ enum TracePoint : int {
   kTrNdWaitNs = 8,  // not a stamp: mean ns a receiving warp of CTA 0 waited for progress words
   kTrNdFreeIn = 9,  // CTA 0: every peer's dispatch inbox is free (the scan follows)
   kTrNdBarrier,     // CTA 0: past the grid barrier of the scan
+  kTrBarrierExit = 15,  // the device barrier's exit (every rank's within a flag latency): aligns
+                        // the ranks' clocks in a trace
   // normal combine: kernel start, CTA 0's pushes done, CTA 0's reduction done, kernel end,
   // CTA 0's last progress word released
   kTrNcStart = 16, kTrNcPushed, kTrNcReduced, kTrNcEnd, kTrNcPublished,

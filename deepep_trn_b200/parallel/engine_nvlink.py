@@ -121,7 +121,7 @@ class NvlinkEngine:
                 'll.combine_send_cta0_stored': d(32, 37), 'll.combine_send_cta0_released': d(32, 38),
                 # raw %globaltimer stamps (ns), to line up the ranks of one node
                 'abs.dispatch_start': t[0], 'abs.dispatch_end': t[6], 'abs.combine_start': t[16],
-                'abs.combine_end': t[19]}
+                'abs.combine_end': t[19], 'abs.barrier_exit': t[15], 'abs.raw': list(t)}
 
     def barrier(self) -> None:
         """Device-side barrier over the EP group (epoch flags in peer memory, bounded wait)."""
