@@ -424,7 +424,7 @@ def bench_ll(args, buf, rank, dev, control, graph: bool = True, hook: bool = Tru
     del gr
     trace = {k: v for k, v in buf.device_trace().items() if k.startswith('ll.')} if args.trace else None
     res = {'tokens_per_rank': T, 'dispatch_fp8_plus_combine_us': round(us, 2), 'cuda_graph': True,
-           'launches_per_iter': 2, 'check': check}
+           'launches_per_iter': 4, 'check': check}
     if trace is not None:
         res['_trace'] = trace   # phase stamps of the last plain replay (printed, not reported)
     if hook:

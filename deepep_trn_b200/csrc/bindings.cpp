@@ -74,8 +74,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nd_dispatch", &nd_dispatch);
   m.def("nc_combine", &nc_combine);
   m.def("ll_dispatch_send", &ll_dispatch_send);
-  m.def("ll_dispatch", &ll_dispatch);
-  m.def("ll_combine", &ll_combine);
   m.def("ll_dispatch_recv", &ll_dispatch_recv);
   m.def("ll_combine_send", &ll_combine_send);
   m.def("ll_combine_recv", &ll_combine_recv);

@@ -59,8 +59,7 @@ constexpr int kMaxGrid = 256;
 
 // Written by peers (remote stores), polled locally.
 struct Signals {
-  uint64_t nd_cnt[B200EP_MAX_RANKS];    // (q << 32) | rows source s sends this rank
-  uint64_t nd_grid[B200EP_MAX_RANKS];   // (q << 32) | CTAs of source s's dispatch kernel
+  uint64_t nd_cnt[B200EP_MAX_RANKS];    // (q << 32) | (source s's CTAs - 1) << 24 | rows s sends this rank
   uint32_t inbox_free[B200EP_MAX_RANKS];   // peer p finished reading its dispatch inbox for dispatch q
   uint32_t cinbox_free[B200EP_MAX_RANKS];  // peer p finished reading its combine inbox for combine q
   uint64_t ll_hdr[2][B200EP_MAX_RANKS];     // (epoch << 32) | num_tokens of source s
@@ -98,9 +97,9 @@ struct HeapLayout {
   int64_t inbox;           // dispatch inbox: [R][M] rows of inbox_stride bytes
   int64_t cinbox_stride;   // bytes per combine inbox row: 16-bit payload, top-k weights
   int64_t cinbox;          // combine inbox: [R][M] rows of cinbox_stride bytes
-  int64_t nd_nte;          // [R][E/R] int32: tokens each source sends to each local expert (written by the sources)
+  int64_t nd_nte;          // [R][E/R] uint64: (q << 32) | tokens each source sends to each local expert
   int64_t nd_rcnt;         // [kMaxGrid][R] int32: rows of each CTA's token range per destination
-  int64_t info;            // [R][kMaxGrid][2] uint64: (q << 32) | first row, (q << 32) | rows of (source, CTA)
+  int64_t info;            // [R][kMaxGrid] uint64: (q & 0xffff) << 48 | first row << 24 | rows of (source, CTA)
   int64_t prog;            // [R][kMaxGrid] uint64: (q << 32) | rows dispatch (source, CTA) has pushed here
   int64_t cprog;           // [R][kMaxGrid] uint64: (q << 32) | rows combine (expert rank, CTA) has pushed here
   // low-latency dispatch receive (x2): [R][Mll] rows, [R][Mll][K] ids
@@ -144,9 +143,9 @@ inline HeapLayout make_layout(const HeapConfig& c, int64_t* guards = nullptr, in
   L.inbox = take(int64_t(c.R) * c.M * L.inbox_stride);
   L.cinbox_stride = cinbox_row_bytes(c.H, c.K);
   L.cinbox = take(int64_t(c.R) * c.M * L.cinbox_stride);
-  L.nd_nte = take(int64_t(c.E) * 4);
+  L.nd_nte = take(int64_t(c.E) * 8);
   L.nd_rcnt = take(int64_t(kMaxGrid) * c.R * 4);
-  L.info = take(int64_t(c.R) * kMaxGrid * 16);
+  L.info = take(int64_t(c.R) * kMaxGrid * 8);
   L.prog = take(int64_t(c.R) * kMaxGrid * 8);
   L.cprog = take(int64_t(c.R) * kMaxGrid * 8);
   for (int b = 0; b < 2; ++b) {

@@ -28,10 +28,6 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
-#include <mutex>
-#include <utility>
-#include <vector>
-
 #include "ops.h"
 
 namespace b200ep {
@@ -414,18 +410,6 @@ __global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecv
   ll_dispatch_recv_body(a, ldv_u32(&a.hv.local()->epoch[kEpLLD]));
 }
 
-// Send and receive in one cooperative launch (no receive hook): every CTA sends its tokens,
-// publishes, then receives, so the receive waits overlap the other CTAs' sends and no kernel
-// boundary sits between the halves. All CTAs are resident (cooperative launch), so a CTA
-// waiting for peers never keeps this GPU's own senders off the SMs.
-template <typename T16>
-__global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_fused_kernel(LLSendArgs s, LLRecvArgs r) {
-  LocalState* ls = s.hv.local();
-  const uint32_t e = ldv_u32(&ls->epoch[kEpLLD]) + 1u;
-  ll_dispatch_send_body<T16>(s, e);
-  finish_epoch(ls, kEpLLD, e, kTrLLSendEnd);
-  ll_dispatch_recv_body(r, e);
-}
 
 static LLRecvArgs ll_recv_args(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_scales,
                                at::Tensor recv_count, at::Tensor src_info, at::Tensor layout_range,
@@ -465,50 +449,6 @@ void ll_dispatch_recv(SymmHeap& heap, at::Tensor recv_x, const OptTensor& recv_s
                                     num_experts, use_fp8, ue8m0, cum_stats, wait_stats);
   ll_dispatch_recv_kernel<<<(a.E / a.hv.R) * a.split, kLLRecvThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
-// True if `grid` CTAs of `fn` at `threads` threads are resident at once on this GPU (the
-// occupancy of each kernel is asked once per process).
-static bool fits_resident(const void* fn, int threads, int grid, int num_sms) {
-  static std::mutex mu;
-  static std::vector<std::pair<const void*, int>> known;
-  int per_sm = -1;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    for (const auto& k : known)
-      if (k.first == fn) per_sm = k.second;
-  }
-  if (per_sm < 0) {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, 0) != cudaSuccess) {
-      (void)cudaGetLastError();
-      per_sm = 0;
-    }
-    std::lock_guard<std::mutex> lock(mu);
-    known.emplace_back(fn, per_sm);
-  }
-  return static_cast<int64_t>(per_sm) * num_sms >= grid;
-}
-
-void ll_dispatch(SymmHeap& heap, const at::Tensor& x, const at::Tensor& topk_idx, int64_t num_experts, bool use_fp8,
-                 bool round_scale, at::Tensor recv_x, const OptTensor& recv_scales, at::Tensor recv_count,
-                 at::Tensor src_info, at::Tensor layout_range, at::Tensor pair_meta, bool ue8m0,
-                 const OptTensor& cum_stats, const OptTensor& wait_stats) {
-  const c10::cuda::CUDAGuard guard(x.device());
-  LLSendArgs sa = ll_send_args(heap, x, topk_idx, num_experts, use_fp8, round_scale);
-  LLRecvArgs ra = ll_recv_args(heap, recv_x, recv_scales, recv_count, src_info, layout_range, pair_meta,
-                               num_experts, use_fp8, ue8m0, cum_stats, wait_stats);
-  const int grid = (ra.E / ra.hv.R) * ra.split;
-  void* fn = x.scalar_type() == at::kHalf ? reinterpret_cast<void*>(ll_dispatch_fused_kernel<__half>)
-                                          : reinterpret_cast<void*>(ll_dispatch_fused_kernel<__nv_bfloat16>);
-  if (!fits_resident(fn, kLLRecvThreads, grid, heap.num_sms())) {
-    ll_dispatch_send(heap, x, topk_idx, num_experts, use_fp8, round_scale, 0);
-    ll_dispatch_recv(heap, recv_x, recv_scales, recv_count, src_info, layout_range, pair_meta, num_experts, use_fp8,
-                     ue8m0, cum_stats, wait_stats);
-    return;
-  }
-  void* args[] = {&sa, &ra};
-  AT_CUDA_CHECK(cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kLLRecvThreads), args, 0,
-                                            at::cuda::getCurrentCUDAStream()));
 }
 
 // ============================================================================ combine send
@@ -749,15 +689,6 @@ __global__ void __launch_bounds__(kLLThreads) ll_combine_recv_kernel(LCRecvArgs 
   ll_combine_recv_body<T16>(a, ldv_u32(&a.hv.local()->epoch[kEpLLC]));
 }
 
-// Send and receive of a combine in one cooperative launch (no receive hook).
-template <typename T16>
-__global__ void __launch_bounds__(kLLThreads) ll_combine_fused_kernel(LCSendArgs s, LCRecvArgs r) {
-  LocalState* ls = s.hv.local();
-  const uint32_t e = ldv_u32(&ls->epoch[kEpLLC]) + 1u;
-  ll_combine_send_body(s, e);
-  finish_epoch(ls, kEpLLC, e, kTrLCSendEnd);
-  ll_combine_recv_body<T16>(r, e);
-}
 
 static LCRecvArgs lc_recv_args(SymmHeap& heap, const at::Tensor& topk_idx, const at::Tensor& topk_w,
                                at::Tensor out) {
@@ -791,25 +722,6 @@ void ll_combine_recv(SymmHeap& heap, const at::Tensor& topk_idx, const at::Tenso
     ll_combine_recv_kernel<__nv_bfloat16><<<a.T, kLLThreads, 0, stream>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   (void)num_sms;
-}
-
-void ll_combine(SymmHeap& heap, const at::Tensor& x, const at::Tensor& recv_count, const at::Tensor& src_info,
-                const at::Tensor& pair_meta, int64_t num_experts, const at::Tensor& topk_idx, const at::Tensor& topk_w,
-                at::Tensor out) {
-  const c10::cuda::CUDAGuard guard(x.device());
-  LCSendArgs sa = lc_send_args(heap, x, recv_count, src_info, pair_meta, num_experts);
-  LCRecvArgs ra = lc_recv_args(heap, topk_idx, topk_w, out);
-  const int grid = heap.num_sms();
-  void* fn = out.scalar_type() == at::kHalf ? reinterpret_cast<void*>(ll_combine_fused_kernel<__half>)
-                                            : reinterpret_cast<void*>(ll_combine_fused_kernel<__nv_bfloat16>);
-  if (!fits_resident(fn, kLLThreads, grid, heap.num_sms())) {
-    ll_combine_send(heap, x, recv_count, src_info, pair_meta, num_experts, 0);
-    ll_combine_recv(heap, topk_idx, topk_w, out, 0);
-    return;
-  }
-  void* args[] = {&sa, &ra};
-  AT_CUDA_CHECK(cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kLLThreads), args, 0,
-                                            at::cuda::getCurrentCUDAStream()));
 }
 
 }  // namespace b200ep

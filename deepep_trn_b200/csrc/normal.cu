@@ -124,6 +124,30 @@ __device__ __forceinline__ int64_t wait_progress(const uint64_t* p, uint32_t q, 
   return static_cast<int64_t>(v & 0xffffffffu);
 }
 
+// Bounded spin until the bits `mask` of a self-tagged control word equal `tag`; the word's
+// other bits are its value, so no acquire follows (nothing else is read on its account).
+// Same polling as wait_tagged. Returns false after recording a timeout.
+__device__ __forceinline__ bool wait_word(const uint64_t* p, uint64_t mask, uint64_t tag, const HeapView& hv,
+                                          uint32_t op, int peer, uint64_t* out) {
+  uint64_t v = ld_relaxed_sys64(p);
+  if ((v & mask) != tag) {
+    const uint64_t t0 = global_ns();
+    uint32_t spins = 0;
+    while (true) {
+      __nanosleep(128);
+      v = ld_relaxed_sys64(p);
+      if ((v & mask) == tag) break;
+      if ((++spins & 15u) == 0u && (global_ns() - t0 > hv.timeout_ns || has_error(hv.status))) {
+        report_error(hv.status, kTimeoutReady, op, hv.rank, peer, static_cast<uint32_t>(tag >> 32),
+                     static_cast<uint32_t>(v >> 32));
+        return false;
+      }
+    }
+  }
+  *out = v;
+  return true;
+}
+
 // Barrier over the CTAs of a cooperative launch (all resident); bounded. Every CTA must
 // call it the same number of times, errors included.
 __device__ bool grid_barrier(LocalState* ls, const HeapView& hv, uint32_t op) {
@@ -444,35 +468,38 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
   __syncthreads();  // s_fail from the inbox waits
   const bool fail0 = s_fail != 0;
   if (!fail0) {
-    // my range's (first row, rows) to every destination; CTA 0 also its totals and per-expert
-    // counts (every destination's row total tells it the size of this source's block)
+    // Control words are self-tagged 64-bit values written with relaxed stores: a word is valid
+    // once its tag is this op's, so no fence orders them and none waits for earlier remote
+    // stores to be acknowledged. (A release behind remote stores completes only after their
+    // acks, which queue behind the peer's own row traffic in the other direction: totals sent
+    // that way reached a busy peer ~120 us late at EP2.) To destination p:
+    //   info[me][b]  (q & 0xffff) << 48 | first row of my range b in p's block << 24 | its rows
+    //   nd_cnt[me]   q << 32 | (my CTAs - 1) << 24 | my rows for p          (CTA 0)
+    //   nd_nte[me][le]  q << 32 | my tokens for p's local expert le         (CTA 0)
     if (tid < R) {
-      uint64_t* info = hv.at<uint64_t>(tid, hv.L.info) + (static_cast<int64_t>(me) * kMaxGrid + b) * 2;
-      st_release_sys64(info, (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(s_start[tid]));
-      st_release_sys64(info + 1, (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(s_cnt[tid]));
+      st_relaxed_sys64(hv.at<uint64_t>(tid, hv.L.info) + static_cast<int64_t>(me) * kMaxGrid + b,
+                       (static_cast<uint64_t>(q & 0xffffu) << 48) |
+                           (static_cast<uint64_t>(s_start[tid]) << 24) | static_cast<uint64_t>(s_cnt[tid]));
+      if (b == 0)
+        st_relaxed_sys64(&hv.sig(tid)->nd_cnt[me], (static_cast<uint64_t>(q) << 32) |
+                                                       (static_cast<uint64_t>(G - 1) << 24) |
+                                                       static_cast<uint64_t>(s_tot[tid]));
     }
     if (b == 0) {
-      if (a.nte)
+      if (a.nte) {
+        const int EL = a.E / R;
         for (int i = tid; i < a.E; i += kThreads) {
-          // destination p gets this rank's counts of p's experts in its own memory, so the
-          // receiver sums them locally (a remote read's reply would queue behind the row
-          // pushes arriving over the same link)
-          const int EL = a.E / R, p = i / EL;
-          hv.at<int32_t>(p, hv.L.nd_nte)[me * EL + (i - p * EL)] = a.nte[i];
+          const int p = i / EL;
+          st_relaxed_sys64(hv.at<uint64_t>(p, hv.L.nd_nte) + me * EL + (i - p * EL),
+                           (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(a.nte[i]));
         }
-      __syncthreads();
-      if (tid < R) {
-        fence_sys();
-        st_release_sys64(&hv.sig(tid)->nd_grid[me], (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(G));
-        st_release_sys64(&hv.sig(tid)->nd_cnt[me], (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(s_tot[tid]));
       }
       if (tid == 0) ls->trace[kTrNdScanned] = global_ns();
     }
   }
-  // Every CTA's control words (its range's first row and rows, CTA 0's totals and per-expert
-  // counts) leave before any CTA pushes rows: queued behind the other CTAs' row traffic, CTA
-  // 0's totals landed ~70 us late at EP2, and a receiver cannot place any row before it has
-  // every source's total. The barrier is taken on every path (errors included).
+  // Every CTA's control words leave before any CTA pushes rows, so they do not queue behind
+  // row traffic: a receiver cannot place any row before it has every source's total. The
+  // barrier is taken on every path (errors included).
   if (!grid_barrier(ls, hv, 2) && tid == 0) s_fail = 1;
   __syncthreads();
   const bool fail1 = s_fail != 0;
@@ -506,16 +533,43 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
   __shared__ int s_rfail;
   if (tid == 0) s_rfail = fail1 ? 1 : 0;
   __syncthreads();
-  if (tid < R && !fail1) {
-    const int64_t c = wait_tagged(&hv.sig(me)->nd_cnt[tid], q, hv, kTimeoutReady, 1, tid);
-    const int64_t g = c < 0 ? -1 : wait_tagged(&hv.sig(me)->nd_grid[tid], q, hv, kTimeoutReady, 1, tid);
-    if (c < 0 || g < 0) {
-      s_rfail = 1;
-      s_rcount[tid] = 0;
-    } else {
-      if (g != G) report_error(hv.status, kBadInput, 1, me, tid, G, static_cast<uint32_t>(g));
-      s_rcount[tid] = static_cast<int32_t>(c);
-      if (g != G) s_rfail = 1;
+  __shared__ int32_t s_istart[B200EP_MAX_RANKS], s_icnt[B200EP_MAX_RANKS];  // source s's range b here
+  if (!fail1) {
+    uint64_t v = 0;
+    if (tid < R) {
+      // source tid's rows for this rank, and its grid size
+      if (!wait_word(&hv.sig(me)->nd_cnt[tid], 0xffffffff00000000ull, static_cast<uint64_t>(q) << 32, hv, 1, tid,
+                     &v)) {
+        s_rfail = 1;
+        s_rcount[tid] = 0;
+      } else {
+        const int g = static_cast<int>((v >> 24) & 0xffu) + 1;
+        s_rcount[tid] = static_cast<int32_t>(v & 0xffffffu);
+        if (g != G) {
+          report_error(hv.status, kBadInput, 1, me, tid, G, static_cast<uint32_t>(g));
+          s_rfail = 1;
+        }
+      }
+    } else if (tid >= 32 && tid < 32 + R) {
+      // source s's range b: first row in block s and rows (another warp polls these)
+      const int s = tid - 32;
+      if (s == me) {
+        s_istart[s] = s_start[me];
+        s_icnt[s] = s_cnt[me];
+      } else if (wait_word(hv.at<uint64_t>(me, hv.L.info) + static_cast<int64_t>(s) * kMaxGrid + b,
+                           0xffff000000000000ull, static_cast<uint64_t>(q & 0xffffu) << 48, hv, 1, s, &v)) {
+        s_istart[s] = static_cast<int32_t>((v >> 24) & 0xffffffu);
+        s_icnt[s] = static_cast<int32_t>(v & 0xffffffu);
+        if (s_istart[s] + s_icnt[s] > M) {  // a range must lie inside the source's block
+          report_error(hv.status, kBadInput, 1, me, s, M, static_cast<uint32_t>(s_istart[s] + s_icnt[s]));
+          s_icnt[s] = 0;
+          s_rfail = 1;
+        }
+      } else {
+        s_istart[s] = 0;
+        s_icnt[s] = 0;
+        s_rfail = 1;
+      }
     }
   }
   __syncthreads();
@@ -543,7 +597,12 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
     for (int le = tid; le < EL && le < 1024; le += kThreads) {
       int32_t sum = 0;
       if (!rfail && a.nte)
-        for (int s = 0; s < R; ++s) sum += ldv_i32(hv.at<int32_t>(me, hv.L.nd_nte) + s * EL + le);
+        for (int s = 0; s < R; ++s) {
+          uint64_t v = 0;
+          if (wait_word(hv.at<uint64_t>(me, hv.L.nd_nte) + s * EL + le, 0xffffffff00000000ull,
+                        static_cast<uint64_t>(q) << 32, hv, 1, s, &v))
+            sum += static_cast<int32_t>(v & 0xffffffffu);
+        }
       host->notify.per_expert[le] = sum;
     }
     if (tid == 0) {
@@ -599,23 +658,17 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
     // rows pushed by other ranks: for each source (rotated), the rows of its CTA b's range
     for (int k = 1; k < R; ++k) {
       const int s = (me + R - k) % R;
-      const uint64_t* info = hv.at<uint64_t>(me, hv.L.info) + (static_cast<int64_t>(s) * kMaxGrid + b) * 2;
-      __shared__ int64_t s_info[2];
+      const int64_t start = s_istart[s], cnt = s_icnt[s];
       if (tid == 0) {
         const uint64_t tw = global_ns();
-        const int64_t c = wait_tagged(info + 1, q, hv, kTimeoutReady, 1, s);
-        s_info[1] = c;
-        s_info[0] = c < 0 ? 0 : static_cast<int64_t>(ld_acquire_sys64(info) & 0xffffffffu);
-        if (c < 0) s_rfail = 1;
         // the whole range lands before its one progress word
-        if (c > 0 && wait_progress(hv.at<uint64_t>(me, hv.L.prog) + static_cast<int64_t>(s) * kMaxGrid + b, q, c,
-                                   hv, 1, s) < 0)
+        if (cnt > 0 && wait_progress(hv.at<uint64_t>(me, hv.L.prog) + static_cast<int64_t>(s) * kMaxGrid + b, q,
+                                     cnt, hv, 1, s) < 0)
           s_rfail = 1;
         waited += global_ns() - tw;
       }
       __syncthreads();  // every thread reads rows that thread 0 acquired
       if (s_rfail) break;
-      const int64_t start = s_info[0], cnt = s_info[1];
       if (tid == 0) {
         a.recv_info[(static_cast<int64_t>(s) * kMaxGrid + b) * 2] = static_cast<int32_t>(start);
         a.recv_info[(static_cast<int64_t>(s) * kMaxGrid + b) * 2 + 1] = static_cast<int32_t>(cnt);
@@ -674,6 +727,7 @@ void nd_dispatch(SymmHeap& heap, const at::Tensor& x, const OptTensor& x_scales,
   TORCH_CHECK(token_pos.is_contiguous() && token_pos.scalar_type() == at::kInt, "token_pos must be int32");
   TORCH_CHECK(recv_off.numel() == hv.R + 1 && recv_off.scalar_type() == at::kLong, "recv_off must be [R+1] int64");
   TORCH_CHECK(num_experts <= hv.cfg.E && num_experts % hv.R == 0, "num_experts exceeds the buffer");
+  TORCH_CHECK(hv.cfg.M < (1 << 24), "at most 2^24 - 1 tokens per rank (24-bit row fields of the control words)");
   NdArgs a{};
   a.hv = hv;
   a.T = static_cast<int>(x.size(0));

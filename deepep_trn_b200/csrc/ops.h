@@ -105,15 +105,6 @@ void ll_combine_send(SymmHeap& heap, const at::Tensor& x, const at::Tensor& recv
                      const at::Tensor& pair_meta, int64_t num_experts, int64_t num_sms);
 void ll_combine_recv(SymmHeap& heap, const at::Tensor& topk_idx, const at::Tensor& topk_w, at::Tensor out,
                      int64_t num_sms);
-// send + receive in one cooperative launch when every CTA fits on the GPU at once (else the
-// two kernels above, back to back)
-void ll_dispatch(SymmHeap& heap, const at::Tensor& x, const at::Tensor& topk_idx, int64_t num_experts, bool use_fp8,
-                 bool round_scale, at::Tensor recv_x, const OptTensor& recv_scales, at::Tensor recv_count,
-                 at::Tensor src_info, at::Tensor layout_range, at::Tensor pair_meta, bool ue8m0,
-                 const OptTensor& cum_stats, const OptTensor& wait_stats);
-void ll_combine(SymmHeap& heap, const at::Tensor& x, const at::Tensor& recv_count, const at::Tensor& src_info,
-                const at::Tensor& pair_meta, int64_t num_experts, const at::Tensor& topk_idx, const at::Tensor& topk_w,
-                at::Tensor out);
 
 // diag.cu
 void device_barrier(SymmHeap& heap);

@@ -9,9 +9,8 @@ One op = one or two kernel launches on the caller's stream:
                           kernel is still moving rows (skipped for a cached dispatch or
                           with num_worst_tokens)
   combine              -> nc_combine (one cooperative kernel: push rows home, fp32 reduce)
-  low_latency_dispatch -> ll_dispatch (send + receive in one cooperative kernel), or with
-                          a receive hook ll_dispatch_send now and ll_dispatch_recv in the hook
-  low_latency_combine  -> ll_combine, or ll_combine_send + ll_combine_recv in the hook
+  low_latency_dispatch -> ll_dispatch_send [+ ll_dispatch_recv, or via the hook]
+  low_latency_combine  -> ll_combine_send  [+ ll_combine_recv, or via the hook]
 
 Low-latency ops never touch the host and are CUDA-graph capturable once the
 heap exists (call them once before capture).
@@ -293,11 +292,9 @@ class NvlinkEngine:
         self._ensure(self._spec(H, K, num_experts, Mll=M))
         Mll = self.spec.max_ll_tokens
         dev = x.device
-        idx = topk_idx.contiguous()
-        if return_recv_hook:
-            with timer.stage('ll_send'):
-                self.C.ll_dispatch_send(self.heap, x, idx, num_experts, bool(use_fp8),
-                                        bool(round_scale or use_ue8m0), self._sms(None))
+        with timer.stage('ll_send'):
+            self.C.ll_dispatch_send(self.heap, x, topk_idx.contiguous(), num_experts, bool(use_fp8),
+                                    bool(round_scale or use_ue8m0), self._sms(None))
         if use_fp8:
             recv_x = torch.empty(EL, R * Mll, H, dtype=torch.float8_e4m3fn, device=dev)
             recv_s = torch.empty(EL, R * Mll, H // 128, dtype=torch.uint8 if use_ue8m0 else torch.float32, device=dev)
@@ -330,18 +327,12 @@ class NvlinkEngine:
                                   pair_meta=pair_meta, use_fp8=bool(use_fp8),
                                   extra=dict(src_info_full=src_info, pair_meta_full=pair_meta))
         self.last_exchange = dict(mode='ll', tokens=T, hidden=H)
+        self._ll_pending = True
         hook = None
         if return_recv_hook:
-            self._ll_pending = True
             hook = _OneShot(recv)
         else:
-            # send and receive in one launch
-            with timer.stage('ll_dispatch'):
-                self.C.ll_dispatch(self.heap, x, idx, num_experts, bool(use_fp8), bool(round_scale or use_ue8m0),
-                                   recv_x, recv_s, recv_count, src_info, layout_range, pair_meta, bool(use_ue8m0),
-                                   cum, wait_stats)
-            if cumulative_stats is not None and cum is None:
-                cumulative_stats.add_(recv_count.to(cumulative_stats.dtype))
+            recv()
         return packed, recv_count, handle, EventOverlap(), hook
 
     def low_latency_combine(self, x, topk_idx, topk_weights, handle, zero_copy, return_recv_hook, out):
@@ -353,18 +344,12 @@ class NvlinkEngine:
         T, H = handle.num_tokens, handle.hidden
         if x.dim() != 3 or x.shape[-1] != H:
             raise ValueError(f'combine x must be [EL, R*M, {H}], got {tuple(x.shape)}')
-        result = out if out is not None else torch.empty(T, H, dtype=x.dtype, device=x.device)
-        idx = topk_idx.contiguous()
-        w = topk_weights.float().contiguous()
-        if not return_recv_hook:
-            # send and receive in one launch
-            with timer.stage('ll_combine'):
-                self.C.ll_combine(self.heap, x, handle.recv_count, handle.extra['src_info_full'],
-                                  handle.extra['pair_meta_full'], handle.num_experts, idx, w, result)
-            return result, EventOverlap(), None
         with timer.stage('ll_send'):
             self.C.ll_combine_send(self.heap, x, handle.recv_count, handle.extra['src_info_full'],
                                    handle.extra['pair_meta_full'], handle.num_experts, self._sms(None))
+        result = out if out is not None else torch.empty(T, H, dtype=x.dtype, device=x.device)
+        idx = topk_idx.contiguous()
+        w = topk_weights.float().contiguous()
 
         def recv():
             with timer.stage('ll_recv'):
@@ -372,7 +357,12 @@ class NvlinkEngine:
             self._lc_pending = False
 
         self._lc_pending = True
-        return result, EventOverlap(), _OneShot(recv)
+        hook = None
+        if return_recv_hook:
+            hook = _OneShot(recv)
+        else:
+            recv()
+        return result, EventOverlap(), hook
 
 
 def _contig(t):

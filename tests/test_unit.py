@@ -192,8 +192,8 @@ def test_heap_layout_regions_fit_and_guards_separate_them(R, M, Mll, H, K, E):
     cins = L['cinbox_stride']
     assert cins % 128 == 0 and cins >= 2 * H + 4 * K                    # 16-bit combine row + weights
     G = L['max_grid']
-    single = {'inbox': R * M * ins, 'cinbox': R * M * cins, 'nd_nte': E * 4, 'nd_rcnt': G * R * 4,
-              'info': R * G * 16, 'prog': R * G * 8, 'cprog': R * G * 8}
+    single = {'inbox': R * M * ins, 'cinbox': R * M * cins, 'nd_nte': E * 8, 'nd_rcnt': G * R * 4,
+              'info': R * G * 8, 'prog': R * G * 8, 'cprog': R * G * 8}
     need = {'ll_rows': R * Mll * rs, 'll_ids': R * Mll * K * 4, 'lc_rows': Mll * K * 2 * H}
     regions = [(L['sig'], L['signals_bytes']), (L['local'], L['local_state_bytes'])]
     regions += [(off, need[name]) for name in need for off in L[name]]
