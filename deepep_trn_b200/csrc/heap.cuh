@@ -60,6 +60,7 @@ constexpr int kMaxGrid = 256;
 // Written by peers (remote stores), polled locally.
 struct Signals {
   uint64_t nd_cnt[B200EP_MAX_RANKS];    // (q << 32) | (source s's CTAs - 1) << 24 | rows s sends this rank
+  uint32_t nd_start[B200EP_MAX_RANKS];     // peer p started dispatch q (a timing signal: orders nothing)
   uint32_t inbox_free[B200EP_MAX_RANKS];   // peer p finished reading its dispatch inbox for dispatch q
   uint32_t cinbox_free[B200EP_MAX_RANKS];  // peer p finished reading its combine inbox for combine q
   uint64_t ll_hdr[2][B200EP_MAX_RANKS];     // (epoch << 32) | num_tokens of source s

@@ -392,6 +392,8 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
     ls->trace[kTrNdStart] = global_ns();
     ls->trace[kTrNdWaitNs] = 0;
   }
+  // CTA 0 tells every peer that this rank entered dispatch q (relaxed: a timing signal only)
+  if (b == 0 && tid < R && tid != me) st_relaxed_sys(&hv.sig(tid)->nd_start[me], q);
   __syncthreads();
   wait_inboxes_free(hv, kEpInbox, q, &s_fail);
   if (b == 0) {  // block-uniform
@@ -411,6 +413,13 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
   __syncthreads();
   int32_t* rcnt = hv.at<int32_t>(me, hv.L.nd_rcnt);
   if (tid < R) rcnt[b * R + tid] = s_cnt[tid];
+  // The ranks start pushing together: CTA 0 holds the grid barrier below until every peer has
+  // entered this dispatch. Without it a rank that finished its previous combine early pushed
+  // alone, then waited for the late rank's rows, and the lead swapped ranks from op to op
+  // (B200, EP2: ~110 us of skew, 0.51 ms per step against 0.32 ms with the ranks in phase).
+  if (b == 0 && tid < R && tid != me &&
+      !wait_epoch(&hv.sig(me)->nd_start[tid], q, hv.timeout_ns, hv.status, kTimeoutReady, 12, me, tid))
+    s_fail = 1;
   if (!grid_barrier(ls, hv, 1) && tid == 0) s_fail = 1;
   if (b == 0 && tid == 0) ls->trace[kTrNdBarrier] = global_ns();
   for (int r = warp; r < R; r += kWarps) {
