@@ -1,5 +1,8 @@
 """Aggregate a results directory into summary.md and ops.csv (reference: bench/report.py).
 
+Reads ``ops_ep*.jsonl`` (bench/bench_ops.py), ``transport_ep*.jsonl``, ``baselines_ep*.jsonl``,
+``moe_ep*.jsonl``, ``gemm.jsonl`` and ``headline_*.jsonl`` (the JSON lines of bench.py).
+
 python bench/report.py results/<run_id>
 """
 from __future__ import annotations
@@ -24,7 +27,9 @@ def med(d):
 def fmt(v):
     if v is None:
         return '-'
-    return f'{v:.2f}' if isinstance(v, float) else str(v)
+    if isinstance(v, float):
+        return f'{v:.4g}' if abs(v) < 10 else f'{v:.2f}'
+    return str(v)
 
 
 def table(header, rows):
@@ -65,6 +70,22 @@ def main():
                  r.get('error', '')] for r in bl]
         parts += ['## NCCL collective baselines', '',
                   table(['op', 'preset', 'EP', 'T/rank', 'pipelined us', 'latency us', 'error'], rows), '']
+    heads = []
+    for path in sorted(run.glob('headline_*.jsonl')):
+        heads += [json.loads(line) for line in path.read_text().splitlines() if line.startswith('{')]
+    if heads:
+        rows = []
+        for r in sorted(heads, key=lambda r: (r.get('impl', ''), r.get('n_gpus', 0), r.get('dtype', ''))):
+            ll, nc, e2e = r.get('ll') or {}, r.get('nccl') or {}, r.get('e2e') or {}
+            roof = (r.get('roofline') or {}).get('of_measured_770')
+            rows.append([r.get('impl'), r.get('n_gpus'), r.get('dtype'), r.get('check'), r.get('ms_per_step'),
+                         r.get('value'), r.get('per_gpu_gbps'), r.get('offrank_gbps_per_gpu'), roof,
+                         nc.get('ms_per_step'), r.get('vs_baseline'), ll.get('dispatch_fp8_plus_combine_us'),
+                         (nc.get('ll') or {}).get('dispatch_fp8_plus_combine_us'), e2e.get('value'),
+                         (r.get('clocks') or {}).get('sm_mhz')])
+        parts += ['## Headline (`bench.py`: 4096 tokens per rank, H=7168, top-8 of 256; LL at 128 tokens)', '',
+                  table(['impl', 'GPUs', 'dtype', 'check', 'ms/step', 'GB/s (sum)', 'GB/s/GPU', 'off-rank GB/s/GPU',
+                         'of 770', 'NCCL ms/step', 'vs NCCL', 'LL us', 'NCCL LL us', 'e2e GB/s', 'SM MHz'], rows), '']
     moe = load(run, 'moe')
     if moe:
         rows = []
