@@ -147,6 +147,25 @@ __device__ __forceinline__ void red_add_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+// For a flag whose writer and readers are on the same GPU (a rank signalling itself) GPU scope
+// suffices; a system-scope fence took ~6 us on B200 even with only local stores outstanding.
+__device__ __forceinline__ void fence_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void red_add_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_gpu64(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Release of a flag at rank `dst`: GPU scope when the flag and its readers are on this GPU.
+__device__ __forceinline__ void signal_add(uint32_t* p, uint32_t v, bool local) {
+  if (local) {
+    fence_gpu();
+    red_add_release_gpu(p, v);
+  } else {
+    fence_sys();
+    red_add_release_sys(p, v);
+  }
+}
 // Orders generic-proxy accesses of this thread with its later async-proxy (TMA) ones.
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");

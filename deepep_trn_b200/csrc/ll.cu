@@ -161,8 +161,7 @@ __device__ void ll_dispatch_send_body(const LLSendArgs& a, uint32_t e) {
   }
   if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLLSendStored] = global_ns();
   if (tid < R && t1 > t0) {
-    fence_sys();
-    red_add_release_sys(&hv.sig(tid)->ll_cnt[slot][me], static_cast<uint32_t>(t1 - t0));
+    signal_add(&hv.sig(tid)->ll_cnt[slot][me], static_cast<uint32_t>(t1 - t0), tid == me);
   }
   if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLLSendReleased] = global_ns();
 }
@@ -363,7 +362,7 @@ __device__ void ll_dispatch_recv_body(const LLRecvArgs& a, uint32_t e) {
       const int t2 = s_tok[q], s2 = s_src[q], p = s_dst[q];
       const uint8_t* row = hv.at<uint8_t>(me, hv.L.ll_rows[slot]) + (static_cast<int64_t>(s2) * Mll + t2) * rs;
       const int64_t o = le * RM + p;
-      warp_copy<16>(a.recv_x + o * PB, row, PB);
+      warp_copy<8>(a.recv_x + o * PB, row, PB);
       if (a.use_fp8) {
         const float* sc = reinterpret_cast<const float*>(row + H);
         if (a.ue8m0) {
@@ -406,7 +405,8 @@ __device__ void ll_dispatch_recv_body(const LLRecvArgs& a, uint32_t e) {
   }
 }
 
-__global__ void __launch_bounds__(kLLRecvThreads) ll_dispatch_recv_kernel(LLRecvArgs a) {
+// two CTAs per SM (<= 64 registers): at EP1 the 256 local experts then fit in one wave
+__global__ void __launch_bounds__(kLLRecvThreads, 2) ll_dispatch_recv_kernel(LLRecvArgs a) {
   ll_dispatch_recv_body(a, ldv_u32(&a.hv.local()->epoch[kEpLLD]));
 }
 
@@ -530,8 +530,7 @@ __device__ void ll_combine_send_body(const LCSendArgs& a, uint32_t e) {
   __syncthreads();
   if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLCSendStored] = global_ns();
   if (tid < R && s_n[tid] > 0) {
-    fence_sys();
-    red_add_release_sys(&hv.sig(tid)->lc_cnt[slot][hv.rank], s_n[tid]);
+    signal_add(&hv.sig(tid)->lc_cnt[slot][hv.rank], s_n[tid], tid == hv.rank);
   }
   if (blockIdx.x == 0 && tid == 0) ls->trace[kTrLCSendReleased] = global_ns();
 }

@@ -941,9 +941,15 @@ __global__ void __launch_bounds__(kThreads, 1) nc_kernel(NcArgs a) {
   if (b == 0 && tid == 0) ls->trace[kTrNcPushed] = global_ns();
   // one release per source covers every row of its range (an empty range too)
   if (!fail0 && tid < R && (tid != me || a.pairs)) {
-    fence_sys();
-    st_release_sys64(hv.at<uint64_t>(tid, hv.L.cprog) + static_cast<int64_t>(me) * kMaxGrid + b,
-                     (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(s_cnt[tid]));
+    uint64_t* pw = hv.at<uint64_t>(tid, hv.L.cprog) + static_cast<int64_t>(me) * kMaxGrid + b;
+    const uint64_t word = (static_cast<uint64_t>(q) << 32) | static_cast<uint32_t>(s_cnt[tid]);
+    if (tid == me) {  // pair mode's own rows: writer and readers on this GPU
+      fence_gpu();
+      st_release_gpu64(pw, word);
+    } else {
+      fence_sys();
+      st_release_sys64(pw, word);
+    }
   }
   if (b == 0 && tid == 0) ls->trace[kTrNcPublished] = global_ns();
   // ---------------------------------------------------------------- wait for this range's rows
