@@ -55,6 +55,7 @@ class NvlinkEngine:
         self.last_exchange = None
         self._last_spec = None
         self._spec_cache: dict = {}
+        self._covered: set = set()   # _spec keys the current heap is known to fit
         self.max_grid = int(self.C.heap_layout(1, 1, 1, 8, 1, 1)['max_grid'])
         if spec_hint is not None:
             self._ensure(spec_hint)
@@ -72,6 +73,7 @@ class NvlinkEngine:
         self.heap = create_heap(self.group, new, self.timeout_s)
         self.spec = new
         self._last_spec = None
+        self._covered = set()
 
     def check(self) -> None:
         """Raise if any kernel of this buffer reported a device-side error."""
@@ -144,9 +146,8 @@ class NvlinkEngine:
             self.heap = None
 
     def _sms(self, config) -> int:
-        from ..buffer import Buffer
         n = getattr(config, 'num_sms', 0) if config is not None else 0
-        return int(n or Buffer.num_sms or 0)
+        return int(n or _buffer_cls().num_sms or 0)
 
     def _grid(self, config) -> int:
         """CTAs of the normal-mode kernels (one per SM by default); every rank must use the same."""
@@ -156,7 +157,11 @@ class NvlinkEngine:
     def _spec(self, H, K, E, Mll=None) -> HeapSpec:
         key = (H, K, E, Mll)
         sp = self._spec_cache.get(key)
+        if sp is not None and key in self._covered:   # the current heap already fits this shape
+            self._last_spec = sp
+            return sp
         if sp is not None and self.spec is not None and self.spec.covers(sp):
+            self._covered.add(key)
             self._last_spec = sp
             return sp
         cur = self.spec
@@ -363,6 +368,17 @@ class NvlinkEngine:
         else:
             recv()
         return result, EventOverlap(), hook
+
+
+_BUFFER = None
+
+
+def _buffer_cls():
+    global _BUFFER
+    if _BUFFER is None:
+        from ..buffer import Buffer
+        _BUFFER = Buffer
+    return _BUFFER
 
 
 def _contig(t):

@@ -23,6 +23,19 @@ from contextlib import contextmanager
 from typing import Callable, Optional
 
 
+class _NullStage:
+    __slots__ = ()
+
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NULL_STAGE = _NullStage()
+
+
 class StageTimer:
     def __init__(self):
         self.enabled = False
@@ -35,11 +48,12 @@ class StageTimer:
         self.totals.clear()
         self._pending.clear()
 
-    @contextmanager
     def stage(self, name: str):
-        if not self.enabled:
-            yield
-            return
+        # disabled (the default): a shared no-op context, no generator per call on the hot path
+        return self._stage(name) if self.enabled else _NULL_STAGE
+
+    @contextmanager
+    def _stage(self, name: str):
         nvtx = _nvtx()
         if nvtx:
             nvtx.range_push(name)
