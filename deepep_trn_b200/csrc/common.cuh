@@ -107,11 +107,6 @@ __device__ __forceinline__ uint64_t ld_acquire_sys64(const uint64_t* p) {
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 __device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -120,15 +115,6 @@ __device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
 __device__ __forceinline__ uint64_t ld_relaxed_sys64(const uint64_t* p) {
   uint64_t v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-// GPU-scope relaxed load: the polling load of a word that a peer GPU writes over NVLink into
-// this GPU's memory (the write lands in this GPU's L2, which these loads read). Pollers use it
-// and finish with one system-scope acquire of the same word, so their spinning issues no
-// system-scope operations on an SM whose other warps are pushing and releasing.
-__device__ __forceinline__ uint64_t ld_relaxed_gpu64(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
