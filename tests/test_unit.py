@@ -218,3 +218,92 @@ def test_heap_fits_the_headline_config_in_a_fixed_budget():
         pytest.skip('extension not built')
     from deepep_trn_b200.parallel.symm import HeapSpec, heap_bytes
     assert heap_bytes(8, HeapSpec(4096, 128, 7168, 8, 256)) < 1.1e9
+
+
+class _FakeNative:
+    """Stands in for the extension's host ops: records the arguments and returns tensors
+    shaped like the real ones (CPU tensors; nothing runs on a device)."""
+
+    def __init__(self, T, H, K, E, R, N, per_expert):
+        self.T, self.H, self.K, self.E, self.R, self.N, self.per_expert = T, H, K, E, R, N, per_expert
+        self.calls = []
+
+    def layout_op(self, idx, E, R, scratch):
+        self.calls.append(('layout', E, R))
+        return (torch.zeros(R, dtype=torch.int32), torch.zeros(E, dtype=torch.int32),
+                torch.zeros(idx.shape[0], R, dtype=torch.bool))
+
+    def dispatch_op(self, heap, x, xs, mode, round_scale, topk, topk_w, nte, itr, E, G, cap, pad, wait, ticket, tmo):
+        self.calls.append(('dispatch', mode, cap, pad, wait, ticket, G))
+        R, K, H = self.R, self.K, x.shape[1]
+        n = self.N if wait else cap
+        rx = torch.zeros(cap, H, dtype=x.dtype if mode == 0 else torch.float8_e4m3fn)[:n]
+        rs = None if mode == 0 else torch.zeros(cap, H // 128)[:n]
+        rt = None if topk is None else torch.full((cap, K), -1, dtype=topk.dtype)[:n]
+        rw = None if topk_w is None else torch.zeros(cap, K)[:n]
+        notify = ([self.N // R] * R + self.per_expert) if wait else []
+        return (rx, rs, rt, rw, torch.zeros(cap, dtype=torch.int64)[:n], torch.zeros(x.shape[0], R, dtype=torch.int32),
+                torch.zeros(G, R, dtype=torch.int32), torch.zeros(R, 256, 2, dtype=torch.int32),
+                torch.zeros(R + 1, dtype=torch.int64), n, notify)
+
+    def combine_op(self, heap, x, w, recv_off, recv_info, token_pos, send_start, b0, b1, G, pp, pw):
+        self.calls.append(('combine', G, pp is not None))
+        out_w = None if w is None else torch.zeros(token_pos.shape[0], w.shape[1])
+        return torch.zeros(token_pos.shape[0], x.shape[1], dtype=x.dtype), out_w
+
+
+class _FakeHeap:
+    num_sms = 148
+
+    def status(self):
+        return (0, 0, 0, 0, 0, 0, 0)
+
+
+def _fake_engine(T=64, H=256, K=4, E=16, R=2, N=96, per_expert=None):
+    from deepep_trn_b200.parallel import engine_nvlink as EN
+    from deepep_trn_b200.parallel.symm import HeapSpec
+    eng = EN.NvlinkEngine.__new__(EN.NvlinkEngine)
+    eng.C = _FakeNative(T, H, K, E, R, N, per_expert or [3, 5, 0, 7, 1, 2, 4, 6][:E // R])
+    eng.heap, eng.R, eng.M, eng.rank, eng.ticket = _FakeHeap(), R, T, 0, 0
+    eng.spec, eng._last_spec, eng._spec_cache, eng._covered = HeapSpec(T, 8, H, K, E), None, {}, set()
+    eng.max_grid, eng.host_timeout_s, eng._scratch, eng.last_exchange = 256, 60.0, None, None
+    return eng
+
+
+def test_nvlink_engine_host_path_with_a_fake_extension():
+    """The NVLink engine's host side (one native call per op): outputs cut to the notified
+    receive size, handle fields, per-expert counts rounded up by expert_alignment, fp8 tuple
+    output, num_worst_tokens (no wait, padded capacity), cached dispatch and combine with pair
+    mode. A fake extension stands in for the kernels, so this runs without a GPU."""
+    T, H, K, E, R, N = 64, 256, 4, 16, 2, 96
+    eng = _fake_engine(T, H, K, E, R, N)
+    x = torch.randn(T, H).to(torch.bfloat16)
+    idx = torch.randint(0, E, (T, K))
+    w = torch.rand(T, K)
+    ntr, nte, itr = eng.get_dispatch_layout(idx, E)
+    assert ntr.shape == (R,) and nte.shape == (E,) and itr.shape == (T, R)
+    rx, rt, rw, per_expert, h, _ = eng.dispatch(x, None, idx, w, itr, E, 4, 0, None, num_tokens_per_expert=nte)
+    assert rx.shape == (N, H) and rt.shape == (N, K) and rw.shape == (N, K)
+    assert per_expert == [4, 8, 0, 8, 4, 4, 4, 8]                         # [3,5,0,7,1,2,4,6] rounded to 4
+    assert h.num_recv == N and h.recv_counts.tolist() == [N // R] * R and h.grid == 148
+    assert eng.C.calls[-1][:5] == ('dispatch', 0, R * T, False, True)    # worst-case outputs, waits
+    # fp8 in-kernel quantisation returns (e4m3, scales)
+    (q, s), *_ = eng.dispatch(x, None, idx, w, itr, E, 1, 0, None, use_fp8=True, num_tokens_per_expert=nte)
+    assert q.dtype == torch.float8_e4m3fn and s.shape == (N, H // 128)
+    # num_worst_tokens: no wait, every output keeps the padded capacity
+    wx, wt, _, pe, wh, _ = eng.dispatch(x, None, idx, w, itr, E, 1, 160, None, num_tokens_per_expert=nte)
+    assert wx.shape[0] == 160 and wt.shape[0] == 160 and wh.num_recv is None and pe is None
+    assert eng.C.calls[-1][2:5] == (160, True, False)
+    # cached dispatch: no top-k outputs, capacity from the handle
+    cx, ct, cw, cpe, ch, _ = eng.dispatch(x, h, None, None, None, E, 1, 0, None)
+    assert cx.shape[0] == N and ct is None and cw is None and cpe is None and ch.num_recv == N
+    # combine: shape check against the handle, weights channel, pair mode
+    out, out_w, _ = eng.combine(torch.zeros(N, H, dtype=torch.bfloat16), h, torch.rand(N, K), (), None)
+    assert out.shape == (T, H) and out_w.shape == (T, K)
+    with pytest.raises(ValueError):
+        eng.combine(torch.zeros(N + 1, H, dtype=torch.bfloat16), h, None, (), None)
+    pp = torch.zeros(N, K, dtype=torch.int64)
+    eng.combine(torch.zeros(N * K, H, dtype=torch.bfloat16), h, None, (), None, pairs=(pp, torch.rand(N, K)))
+    assert eng.C.calls[-1] == ('combine', 148, True)
+    tickets = [c[5] for c in eng.C.calls if c[0] == 'dispatch']
+    assert tickets == sorted(set(tickets))                               # a fresh ticket per dispatch
