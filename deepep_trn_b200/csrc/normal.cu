@@ -7,10 +7,13 @@
 // is one cooperative kernel in which sending and receiving overlap row by row.
 //
 // Dispatch (nd_kernel), CTA b of G owns source tokens [T*b/G, T*(b+1)/G):
-//   1. scan: the CTA counts its range's rows per destination; after a grid barrier
+//   1. scan: the CTA counts its range's rows per destination; after a grid barrier (held
+//      by CTA 0 until every peer has entered this dispatch, so the ranks push together)
 //      every CTA knows where its range starts in each destination's block, writes the
-//      token -> row map (token_pos) and tells each destination (first row, rows) of
-//      its range; CTA 0 publishes this rank's row totals to every destination.
+//      token -> row map (token_pos) and sends each destination (first row, rows) of its
+//      range; CTA 0 sends this rank's row totals and per-expert counts. These control
+//      words are self-tagged and sent with relaxed stores before any row (second grid
+//      barrier).
 //   2. push (every warp): each token row goes straight from x to every other rank that
 //      owns one of its experts, 16-byte stores into that rank's inbox over NVLink
 //      (fp8 e4m3 + 1x128 scales quantised in registers on the way when asked), with
@@ -21,7 +24,7 @@
 //      that s's CTA b pushed (once its progress word is in) from the inbox to recv_x
 //      at recv_off[s] + row, with the metadata. Rows a rank keeps come from x directly.
 // Combine (nc_kernel), same grid and the same ranges: expert rank r's CTA b pushes the
-// rows of every source s's range b back into s's inbox (weights appended) and publishes;
+// rows of every source s's range b back into s's combine inbox (weights appended) and publishes;
 // then source s's CTA b reduces the tokens of range b in fp32 as their rows are in (own
 // rows read from x in place), adds the optional bias and casts once. The CTAs of a GPU
 // are not in step, so some push while others already receive.
