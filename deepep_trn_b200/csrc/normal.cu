@@ -419,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1) nd_kernel(NdArgs a) {
   // The ranks start pushing together: CTA 0 holds the grid barrier below until every peer has
   // entered this dispatch. Without it a rank that finished its previous combine early pushed
   // alone, then waited for the late rank's rows, and the lead swapped ranks from op to op
-  // (B200, EP2: ~110 us of skew, 0.51 ms per step against 0.32 ms with the ranks in phase).
+  // (B200, EP2: ~110 us of skew, 0.51 ms per step against 0.31 ms with the ranks in phase).
   if (b == 0 && tid < R && tid != me &&
       !wait_epoch(&hv.sig(me)->nd_start[tid], q, hv.timeout_ns, hv.status, kTimeoutReady, 12, me, tid))
     s_fail = 1;
